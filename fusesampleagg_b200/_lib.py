@@ -1,0 +1,90 @@
+"""ctypes binding of libfsa_sm100.so (C ABI in include/fsa_sm100.h).
+
+The library is required: importing this module raises ImportError when it is
+missing or fails to load.  There is no CPU or eager fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libfsa_sm100.so"
+
+FSA_OK = 0
+FSA_ERR_INVALID_ARGUMENT = 1
+FSA_ERR_CUDA = 2
+
+FSA_STATUS_BAD_ROOT = 0x1
+FSA_STATUS_BAD_ROW = 0x2
+FSA_STATUS_BAD_NEIGHBOR = 0x4
+
+MAX_FANOUT_1HOP = 1024
+MAX_2HOP_ENTRIES = 12000
+
+# Every symbol include/fsa_sm100.h declares, with (restype, argtypes).
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_u64 = ctypes.c_uint64
+_int = ctypes.c_int
+
+SIGNATURES = {
+    "fsa_sample_agg_forward": (
+        _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _u64, _p, _p, _p, _p]),
+    "fsa_sample_agg_backward": (
+        _int, [_p, _p, _p, _i64, _i64, _i32, _p, _i64, _p]),
+    "fsa_sample_agg_2hop_forward": (
+        _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p, _p]),
+    "fsa_sample_agg_2hop_backward": (
+        _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p]),
+    "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),
+    "fsa_status_string": (ctypes.c_char_p, [_int]),
+    "fsa_last_cuda_error": (_int, []),
+    "fsa_launch_count": (_u64, []),
+    "fsa_device_status": (_int, [_int, ctypes.POINTER(ctypes.c_uint32), _int]),
+}
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH.name} is not built; run `python -m fusesampleagg_b200.build` "
+            "(nvcc with sm_100a) before importing fusesampleagg_b200"
+        )
+    try:
+        lib = ctypes.CDLL(str(LIB_PATH))
+    except OSError as exc:
+        raise ImportError(f"failed to load {LIB_PATH}: {exc}") from exc
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    return lib
+
+
+LIB = _load()
+
+
+def check(status: int, what: str) -> None:
+    """Raises RuntimeError for a non-zero status of entry point `what`."""
+    if status == FSA_OK:
+        return
+    text = LIB.fsa_status_string(status).decode()
+    if status == FSA_ERR_CUDA:
+        code = LIB.fsa_last_cuda_error()
+        raise RuntimeError(f"{what} failed: {text} (cudaError {code})")
+    raise RuntimeError(f"{what} failed: {text}")
+
+
+def launch_count() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(LIB.fsa_launch_count())
+
+
+def device_status(device: int, reset: bool = True) -> int:
+    """Status word of `device` (FSA_STATUS_* bits); synchronises the device."""
+    flags = ctypes.c_uint32(0)
+    check(LIB.fsa_device_status(int(device), ctypes.byref(flags), int(bool(reset))),
+          "fsa_device_status")
+    return int(flags.value)

@@ -1,0 +1,137 @@
+/*
+ * fsa_sm100.h - C ABI of the B200 (sm_100a) fused reservoir-sample + mean
+ * aggregate operator (libfsa_sm100.so).
+ *
+ * Each compute entry point replaces one host launcher of the reference
+ * (declared at fuseop/binding.cpp:57-72, defined at
+ * fuseop/fused_sample_agg.cu:275-326).  Differences from those launchers:
+ *   - plain C types only; the stream is passed as `void*` (a cudaStream_t);
+ *   - an int status is returned instead of throwing (0 = FSA_OK);
+ *   - `num_nodes` / `num_edges` are passed so every root, row and neighbour
+ *     id is bounds-checked on the device (bad ids are skipped and flagged in
+ *     the per-device status word instead of being dereferenced);
+ *   - `batch_offset` is added to the batch index that seeds first-hop rows,
+ *     so a slice [offset, offset+B) of a larger batch draws exactly the
+ *     samples the whole batch would (multi-GPU root partitioning).
+ *
+ * Layouts: rowptr int32[num_nodes+1], col int32[num_edges] (CSR, neighbour
+ * order within a row is significant), x float32[num_nodes][feature_dim]
+ * row-major, frontier int32[batch_size].  All pointers are device pointers.
+ * Calls are asynchronous and stream-ordered; nothing is allocated and the
+ * host is never synchronised (except fsa_device_status).
+ */
+#ifndef FSA_SM100_H_
+#define FSA_SM100_H_
+
+#include <stdint.h>
+
+#if defined(FSA_BUILD_SHARED)
+#define FSA_API __attribute__((visibility("default")))
+#else
+#define FSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define FSA_OK 0
+#define FSA_ERR_INVALID_ARGUMENT 1 /* a size / fanout / pointer check failed */
+#define FSA_ERR_CUDA 2             /* a CUDA runtime call failed; see fsa_last_cuda_error */
+
+/* Limits, same values as the reference (fuseop/binding.cpp:13-14). */
+#define FSA_MAX_FANOUT_1HOP 1024
+#define FSA_MAX_2HOP_ENTRIES 12000 /* fanout1 + fanout1 * fanout2 */
+
+/* Bits of the per-device status word (fsa_device_status). */
+#define FSA_STATUS_BAD_ROOT 0x1u     /* frontier id outside [0, num_nodes) */
+#define FSA_STATUS_BAD_ROW 0x2u      /* rowptr[r] .. rowptr[r+1] not within [0, num_edges] */
+#define FSA_STATUS_BAD_NEIGHBOR 0x4u /* sampled id outside [0, num_nodes) */
+
+/*
+ * 1-hop forward.  Replaces fused_sample_agg_cuda_forward
+ * (fuseop/fused_sample_agg.cu:275-289; kernel :58-104).
+ * out[b,:] = mean of x over the reservoir sample of row(frontier[b]).
+ * samples int32[batch_size][fanout] (-1 padded) and takes int32[batch_size]
+ * are optional (NULL = not written).  batch_size == 0 or fanout == 0 is a
+ * no-op (the caller owns zero-initialisation of outputs in that case).
+ */
+FSA_API int fsa_sample_agg_forward(const int32_t* rowptr, const int32_t* col,
+                           int64_t num_nodes, int64_t num_edges,
+                           const float* x, int64_t feature_dim,
+                           const int32_t* frontier, int64_t batch_size,
+                           int64_t batch_offset, int32_t fanout, uint64_t seed,
+                           float* out, int32_t* samples, int32_t* takes,
+                           void* stream);
+
+/*
+ * 1-hop backward (saved-index replay).  Replaces
+ * fused_sample_agg_cuda_backward (fuseop/fused_sample_agg.cu:291-301;
+ * kernel :106-132).  grad_x[samples[b,i],:] += grad_out[b,:] / takes[b] for
+ * i < takes[b].  grad_x float32[num_nodes][feature_dim] must be zeroed (or
+ * hold a gradient to accumulate into) by the caller, e.g. with
+ * fsa_fill_zero_f32.
+ */
+FSA_API int fsa_sample_agg_backward(const int32_t* samples, const int32_t* takes,
+                            const float* grad_out, int64_t batch_size,
+                            int64_t feature_dim, int32_t fanout, float* grad_x,
+                            int64_t num_nodes, void* stream);
+
+/*
+ * 2-hop forward.  Replaces fused_sample_agg_2hop_cuda_forward
+ * (fuseop/fused_sample_agg.cu:303-315; kernel :134-214).
+ * out[b,:] = mean over non-empty first-hop slots i of (mean over valid
+ * second-hop slots j of x[samples2[b,i,j],:]).  samples1
+ * int32[batch_size][fanout1] and samples2 int32[batch_size][fanout1][fanout2]
+ * are optional (NULL = not written).
+ */
+FSA_API int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
+                                int64_t num_nodes, int64_t num_edges,
+                                const float* x, int64_t feature_dim,
+                                const int32_t* frontier, int64_t batch_size,
+                                int64_t batch_offset, int32_t fanout1,
+                                int32_t fanout2, uint64_t seed, float* out,
+                                int32_t* samples1, int32_t* samples2,
+                                void* stream);
+
+/*
+ * 2-hop backward (saved-index replay).  Replaces
+ * fused_sample_agg_2hop_cuda_backward (fuseop/fused_sample_agg.cu:317-326;
+ * kernel :216-271).  grad_x[samples2[b,i,j],:] +=
+ * (grad_out[b,:] / nonempty_b) / valid_{b,i}.  grad_x must be pre-zeroed (or
+ * accumulate into an existing gradient).
+ */
+FSA_API int fsa_sample_agg_2hop_backward(const float* grad_out, const int32_t* samples1,
+                                 const int32_t* samples2, int64_t batch_size,
+                                 int64_t feature_dim, int32_t fanout1,
+                                 int32_t fanout2, float* grad_x,
+                                 int64_t num_nodes, void* stream);
+
+/*
+ * Zero count floats at dst.  Replaces the dense gradient allocation fill
+ * at::zeros({N, D}) of the reference backward (fuseop/binding.cpp:137, :220).
+ */
+FSA_API int fsa_fill_zero_f32(float* dst, int64_t count, void* stream);
+
+/* Human-readable text for a status code (static storage). */
+FSA_API const char* fsa_status_string(int status);
+
+/* The cudaError_t of the most recent FSA_ERR_CUDA on this thread (0 if none). */
+FSA_API int fsa_last_cuda_error(void);
+
+/* Number of kernels this library has launched in the process (all threads). */
+FSA_API uint64_t fsa_launch_count(void);
+
+/*
+ * Read (and optionally clear) the status word of `device`: an OR of
+ * FSA_STATUS_* bits set by kernels that met out-of-range ids.  Synchronises
+ * the device; meant for tests and debugging, not the hot path.
+ */
+FSA_API int fsa_device_status(int device, uint32_t* flags, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FSA_SM100_H_ */

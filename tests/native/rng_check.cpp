@@ -1,0 +1,27 @@
+// Host check of fusesampleagg_b200/csrc/fsa_rng.cuh (compiled with g++ by
+// tests/test_rng_host.py): reads "state steps" / "draw value bound" queries
+// on stdin and prints the header's jump-ahead / bounded-draw results.
+#include <cstdio>
+#include <cstring>
+
+#include "fsa_rng.cuh"
+
+static const fsa::JumpTables kTables = fsa::make_jump_tables();
+
+int main() {
+  char op[16];
+  unsigned long long a = 0, b = 0;
+  while (std::scanf("%15s %llu %llu", op, &a, &b) == 3) {
+    if (std::strcmp(op, "jump") == 0) {
+      std::printf("%llu\n", static_cast<unsigned long long>(fsa::jump_host(kTables, a, b)));
+    } else if (std::strcmp(op, "draw") == 0) {
+      std::printf("%u\n", fsa::bounded_draw(a, static_cast<uint32_t>(b)));
+    } else if (std::strcmp(op, "seed") == 0) {
+      // a = base, b = root; hop 1, pos 3 (fixed) and hop 0, pos b
+      std::printf("%llu %llu\n",
+                  static_cast<unsigned long long>(fsa::row_state(a, b, 1, 3)),
+                  static_cast<unsigned long long>(fsa::row_state(a, b, 0, b)));
+    }
+  }
+  return 0;
+}

@@ -1,0 +1,109 @@
+"""The C-ABI library loads without a GPU, exports every symbol that
+include/fsa_sm100.h declares, and rejects bad arguments before touching CUDA."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from fusesampleagg_b200 import _lib
+
+REPO = Path(__file__).resolve().parents[1]
+HEADERS = sorted((REPO / "include").glob("*.h"))
+
+
+def declared_symbols() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        text = h.read_text()
+        names |= set(re.findall(r"FSA_API\s+[\w\s\*]+?\b(fsa_\w+)\s*\(", text))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for required in ("fsa_sample_agg_forward", "fsa_sample_agg_backward",
+                     "fsa_sample_agg_2hop_forward", "fsa_sample_agg_2hop_backward",
+                     "fsa_fill_zero_f32"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_every_declared_symbol():
+    assert declared_symbols() == set(_lib.SIGNATURES)
+
+
+def test_header_compiles_as_c(tmp_path):
+    import subprocess
+
+    src = tmp_path / "t.c"
+    src.write_text('#include "fsa_sm100.h"\nint main(void){return FSA_OK;}\n')
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", f"-I{REPO / 'include'}", "-c",
+                    str(src), "-o", str(tmp_path / "t.o")], check=True)
+
+
+L = _lib.LIB
+NULL = None
+
+
+@pytest.mark.parametrize("fanout", [-1, 1025])
+def test_forward_rejects_bad_fanout(fanout):
+    assert L.fsa_sample_agg_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 4, 0, fanout, 1,
+                                    NULL, NULL, NULL, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+
+
+def test_zero_sized_calls_are_noops_without_cuda():
+    assert L.fsa_sample_agg_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 0, 0, 3, 1,
+                                    NULL, NULL, NULL, NULL) == _lib.FSA_OK
+    assert L.fsa_sample_agg_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, 0, 0, 1,
+                                    NULL, NULL, NULL, NULL) == _lib.FSA_OK
+    assert L.fsa_sample_agg_2hop_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, 0, 0, 3, 1,
+                                         NULL, NULL, NULL, NULL) == _lib.FSA_OK
+    assert L.fsa_sample_agg_2hop_backward(NULL, NULL, NULL, 0, 4, 3, 2, NULL, 10,
+                                          NULL) == _lib.FSA_OK
+    assert L.fsa_fill_zero_f32(NULL, 0, NULL) == _lib.FSA_OK
+
+
+@pytest.mark.parametrize("f1,f2", [(-1, 2), (2, -1), (12000, 1), (1000, 12)])
+def test_2hop_rejects_bad_fanouts(f1, f2):
+    assert L.fsa_sample_agg_2hop_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, 0, f1, f2, 1,
+                                         NULL, NULL, NULL, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert L.fsa_sample_agg_2hop_backward(NULL, NULL, NULL, 5, 4, f1, f2, NULL, 10,
+                                          NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+
+
+def test_null_required_pointers_rejected():
+    assert L.fsa_sample_agg_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, 0, 3, 1,
+                                    NULL, NULL, NULL, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert L.fsa_fill_zero_f32(NULL, 16, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert L.fsa_fill_zero_f32(NULL, -1, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+
+
+def test_negative_sizes_rejected():
+    assert L.fsa_sample_agg_forward(NULL, NULL, -1, 10, NULL, 4, NULL, 5, 0, 3, 1,
+                                    NULL, NULL, NULL, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert L.fsa_sample_agg_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, -3, 3, 1,
+                                    NULL, NULL, NULL, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert L.fsa_sample_agg_backward(NULL, NULL, NULL, -1, 4, 3, NULL, 10,
+                                     NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+
+
+def test_status_strings():
+    assert L.fsa_status_string(0) == b"ok"
+    assert L.fsa_status_string(1) == b"invalid argument"
+    assert L.fsa_status_string(2) == b"CUDA runtime error"
+    assert L.fsa_status_string(99) == b"unknown status"
+
+
+def test_check_raises_runtime_error():
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        _lib.check(_lib.FSA_ERR_INVALID_ARGUMENT, "x")
+    _lib.check(_lib.FSA_OK, "x")
