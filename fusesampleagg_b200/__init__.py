@@ -20,6 +20,8 @@ draws exactly the samples the whole batch would.
 
 from __future__ import annotations
 
+import functools
+
 import torch
 
 from . import _lib
@@ -137,6 +139,68 @@ def _ptr(t):
     return t.data_ptr() if t is not None else None
 
 
+_SIDE_STREAMS: dict[int, torch.cuda.Stream] = {}
+_PRIORITY_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    s = _SIDE_STREAMS.get(idx)
+    if s is None:
+        s = torch.cuda.Stream(device=idx)
+        _SIDE_STREAMS[idx] = s
+    return s
+
+
+def _priority_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    s = _PRIORITY_STREAMS.get(idx)
+    if s is None:
+        s = torch.cuda.Stream(device=idx, priority=-1)
+        _PRIORITY_STREAMS[idx] = s
+    return s
+
+
+def _zeroed(num_nodes: int, dim: int, device: torch.device, stream: int) -> torch.Tensor:
+    grad = torch.empty((num_nodes, dim), dtype=torch.float32, device=device)
+    _lib.check(_L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fsa_fill_zero_f32")
+    return grad
+
+
+class _PendingGrad:
+    """A dense gradient buffer whose zero-fill was launched on a side stream
+    during the forward, so that the memory-bound fill overlaps the
+    compute-bound sampling kernels; the backward waits for it and scatters
+    into it (the reference allocates it with at::zeros inside the backward,
+    fuseop/binding.cpp:137, :220)."""
+
+    __slots__ = ("grad", "done")
+
+    def __init__(self, num_nodes: int, dim: int, device: torch.device):
+        cur = torch.cuda.current_stream(device)
+        side = _side_stream(device)
+        self.grad = torch.empty((num_nodes, dim), dtype=torch.float32, device=device)
+        side.wait_stream(cur)  # the block may have been in use on `cur`
+        _lib.check(_L.fsa_fill_zero_f32(self.grad.data_ptr(), self.grad.numel(),
+                                        side.cuda_stream), "fsa_fill_zero_f32")
+        self.grad.record_stream(side)
+        self.done = torch.cuda.Event()
+        self.done.record(side)
+
+    def take(self) -> torch.Tensor:
+        torch.cuda.current_stream(self.grad.device).wait_event(self.done)
+        g, self.grad = self.grad, None
+        return g
+
+
+def _grad_buffer(zeroed, num_nodes, dim, device, stream) -> torch.Tensor:
+    if zeroed is not None:
+        g = zeroed.take()
+        if tuple(g.shape) == (num_nodes, dim) and g.device == device:
+            return g
+    return _zeroed(num_nodes, dim, device, stream)
+
+
 # ---------------------------------------------------------------------------
 # Launch wrappers (the binding layer, fuseop/binding.cpp:74-231)
 # ---------------------------------------------------------------------------
@@ -165,7 +229,7 @@ def _forward_1hop(rowptr, col, x, frontier, fanout, seed, capture, batch_offset=
     return out, samples, takes
 
 
-def _backward_1hop(samples, takes, grad_out, num_nodes):
+def _backward_1hop(samples, takes, grad_out, num_nodes, zeroed=None):
     if not (samples.is_cuda and takes.is_cuda and grad_out.is_cuda):
         raise RuntimeError("backward inputs must be CUDA tensors")
     if samples.dtype != torch.int32 or takes.dtype != torch.int32:
@@ -185,9 +249,7 @@ def _backward_1hop(samples, takes, grad_out, num_nodes):
     B, D = grad_out.shape
     with _DeviceGuard(grad_out.device):
         stream = _stream_handle(grad_out.device)
-        grad_x = torch.empty((num_nodes, D), dtype=grad_out.dtype, device=grad_out.device)
-        _lib.check(_L.fsa_fill_zero_f32(grad_x.data_ptr(), grad_x.numel(), stream),
-                   "fsa_fill_zero_f32")
+        grad_x = _grad_buffer(zeroed, num_nodes, D, grad_out.device, stream)
         if B == 0 or samples.size(1) == 0:
             return grad_x
         status = _L.fsa_sample_agg_backward(
@@ -197,7 +259,8 @@ def _backward_1hop(samples, takes, grad_out, num_nodes):
     return grad_x
 
 
-def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, batch_offset=0):
+def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, batch_offset=0,
+                  overlap=False):
     _check_graph_inputs(rowptr, col, x, frontier)
     fanout1 = _as_int64(fanout1, "fanout1")
     fanout2 = _as_int64(fanout2, "fanout2")
@@ -215,15 +278,32 @@ def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, bat
         out = torch.empty((B, D), dtype=x.dtype, device=dev)
         s1 = torch.empty((B, fanout1), dtype=torch.int32, device=dev) if capture else None
         s2 = torch.empty((B, fanout1, fanout2), dtype=torch.int32, device=dev) if capture else None
-        status = _L.fsa_sample_agg_2hop_forward(
+        ws_bytes = _L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, D, int(capture),
+                                                         int(capture))
+        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+        launch = functools.partial(
+            _L.fsa_sample_agg_2hop_forward,
             rowptr.data_ptr(), col.data_ptr(), x.size(0), col.numel(), x.data_ptr(), D,
             frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(), _ptr(s1),
-            _ptr(s2), _stream_handle(dev))
+            _ptr(s2), ws.data_ptr(), ws_bytes)
+        if overlap:
+            # While the gradient zero-fill runs on a side stream, launch the
+            # sampling kernels on a high-priority stream so that the block
+            # scheduler prefers them over the fill's CTAs.  Outputs and
+            # workspace were allocated on the caller's stream, which waits for
+            # this work before anything after the call.
+            cur = torch.cuda.current_stream(dev)
+            hi = _priority_stream(dev)
+            hi.wait_stream(cur)
+            status = launch(hi.cuda_stream)
+            cur.wait_stream(hi)
+        else:
+            status = launch(_stream_handle(dev))
         _lib.check(status, "fsa_sample_agg_2hop_forward")
     return out, s1, s2
 
 
-def _backward_2hop(grad_out, samples1, samples2, num_nodes):
+def _backward_2hop(grad_out, samples1, samples2, num_nodes, zeroed=None):
     if not (grad_out.is_cuda and samples1.is_cuda and samples2.is_cuda):
         raise RuntimeError("backward inputs must be CUDA tensors")
     if (grad_out.dtype != torch.float32 or samples1.dtype != torch.int32
@@ -244,9 +324,7 @@ def _backward_2hop(grad_out, samples1, samples2, num_nodes):
     f1, f2 = samples1.size(1), samples2.size(2)
     with _DeviceGuard(grad_out.device):
         stream = _stream_handle(grad_out.device)
-        grad_x = torch.empty((num_nodes, D), dtype=grad_out.dtype, device=grad_out.device)
-        _lib.check(_L.fsa_fill_zero_f32(grad_x.data_ptr(), grad_x.numel(), stream),
-                   "fsa_fill_zero_f32")
+        grad_x = _grad_buffer(zeroed, num_nodes, D, grad_out.device, stream)
         if B == 0 or f1 == 0 or f2 == 0:
             return grad_x
         status = _L.fsa_sample_agg_2hop_backward(
@@ -268,9 +346,12 @@ class _FusedSampleAggFn(torch.autograd.Function):
         out, samples, takes = _forward_1hop(
             rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
             fanout, replay_seed, capture, batch_offset)
+        ctx.pending = None
         if capture:
             ctx.save_for_backward(samples, takes)
             ctx.num_nodes = int(x.size(0))
+            if ctx.needs_input_grad[2]:
+                ctx.pending = _PendingGrad(ctx.num_nodes, x.size(1), x.device)
         ctx.capture = capture
         return out
 
@@ -279,7 +360,9 @@ class _FusedSampleAggFn(torch.autograd.Function):
         grad_x = None
         if ctx.capture and ctx.needs_input_grad[2]:
             samples, takes = ctx.saved_tensors
-            grad_x = _backward_1hop(samples, takes, grad_out.contiguous(), ctx.num_nodes)
+            grad_x = _backward_1hop(samples, takes, grad_out.contiguous(), ctx.num_nodes,
+                                    ctx.pending)
+        ctx.pending = None
         return None, None, grad_x, None, None, None, None, None
 
 
@@ -289,9 +372,13 @@ class _FusedSampleAgg2HopFn(torch.autograd.Function):
                 batch_offset):
         _check_python_inputs(rowptr, col, x, frontier)
         capture = bool(save_indices) or x.requires_grad
+        ctx.pending = None
+        prefill = capture and ctx.needs_input_grad[2]
+        if prefill:
+            ctx.pending = _PendingGrad(int(x.size(0)), x.size(1), x.device)
         out, s1, s2 = _forward_2hop(
             rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
-            fanout1, fanout2, replay_seed, capture, batch_offset)
+            fanout1, fanout2, replay_seed, capture, batch_offset, overlap=prefill)
         if capture:
             ctx.save_for_backward(s1, s2)
             ctx.num_nodes = int(x.size(0))
@@ -303,7 +390,8 @@ class _FusedSampleAgg2HopFn(torch.autograd.Function):
         grad_x = None
         if ctx.capture and ctx.needs_input_grad[2]:
             s1, s2 = ctx.saved_tensors
-            grad_x = _backward_2hop(grad_out.contiguous(), s1, s2, ctx.num_nodes)
+            grad_x = _backward_2hop(grad_out.contiguous(), s1, s2, ctx.num_nodes, ctx.pending)
+        ctx.pending = None
         return None, None, grad_x, None, None, None, None, None, None
 
 

@@ -1,34 +1,35 @@
 // Fused reservoir-sample + mean-aggregate kernels for B200 (sm_100a) and the
 // C ABI declared in include/fsa_sm100.h.
 //
-// Design (see the reference kernels at fuseop/fused_sample_agg.cu:58-271):
+// Reference kernels: fuseop/fused_sample_agg.cu:58-271.  The reference runs
+// Algorithm R on one thread per row (fused_sample_agg.cu:40-56): for
+// power-law graphs that is tens of thousands of dependent xorshift steps per
+// root while the rest of the CTA idles.  Here:
 //
-//   * One CTA per root.  The reference runs Algorithm R on a single thread
-//     per row (fused_sample_agg.cu:40-56), which for power-law graphs means
-//     tens of thousands of dependent xorshift steps per root while the rest
-//     of the CTA idles.  Here the draws of a row are split into contiguous
-//     per-thread chunks; a thread reaches the first state of its chunk with
-//     a GF(2) jump (fsa_rng.cuh) and records, for every reservoir slot, the
-//     largest draw index that replaced it (shared-memory atomicMax).  The
-//     slot's final neighbour is col[winner] or, if never replaced,
-//     col[slot] -- exactly what the serial loop leaves behind, so sampled
-//     ids are bit-identical.
-//   * 2-hop: the draws of all fanout1 second-hop rows of a root form one
-//     concatenated sequence that the whole CTA splits evenly, so a hub
-//     middle does not serialise the root.
-//   * Gather: every (first-hop slot, feature vector) pair is one work item
-//     that sums its valid leaf rows with 128-bit (or 64/32-bit, by feature
-//     width) non-allocating loads in the reference's j order and divides by
-//     the valid count; the per-slot means are then summed in i order.  The
-//     arithmetic order equals the reference's, so forward outputs are
-//     bit-identical too.
-//   * Backward: red.global.add.v4.f32 (v2/scalar for narrow rows) of
-//     (grad/nonempty)/valid into grad_x, one CTA per root.
-//   * No kernel allocates, synchronises or spins.  Out-of-range ids are never
-//     dereferenced: they are skipped and reported in a per-device status word.
+//   * Parallel, bit-exact Algorithm R.  A row's draws are cut into chunks of
+//     kChunk positions aligned to the row start.  A thread reaches a chunk's
+//     first state with GF(2) table products (fsa_rng.cuh), runs its draws and
+//     records, per reservoir slot, the largest position that selected it
+//     (atomicMax).  The slot then holds col[winner], or col[slot] if never
+//     replaced -- exactly what the serial loop leaves behind.
+//   * 2-hop forward = four launches: plan (CTA per root: first hop, table of
+//     second-hop rows), scan (one CTA: chunk prefix over all second-hop
+//     rows), draws (persistent grid; warps take 32 chunks at a time from a
+//     global counter, so hub rows and light rows balance across the GPU) and
+//     gather (one warp per (root, first-hop slot), no CTA barriers; the last
+//     warp of a root sums the slot means).
+//   * Gather order = the reference's: per feature, leaves in j order from
+//     0.0f, / valid; slot means in i order, / non-empty (IEEE division), so
+//     forward outputs are bit-identical.  Rows are read with
+//     ld.global.nc.L1::no_allocate.v{4,2,1}.f32 by feature width.
+//   * Backward: red.global.add.v{4,2}.f32 of (grad/nonempty)/valid.
+//   * No kernel allocates, synchronises with the host or waits on another
+//     thread block.  Out-of-range ids are never dereferenced: they are skipped
+//     and reported in a per-device status word.
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <climits>
 #include <cstdint>
 
 #include "fsa_rng.cuh"
@@ -42,15 +43,12 @@ __device__ constexpr JumpTables g_jump = fsa::make_jump_tables();
 __device__ unsigned int g_status;
 
 constexpr int kThreads1Hop = 128;
-constexpr int kThreads2Hop = 256;
 constexpr int kThreadsBwd = 256;
 constexpr int kThreadsFill = 256;
-// Fewest draws a thread is given before more threads join a row: below this
-// the jump to the chunk start costs more than the draws it parallelises.
-constexpr long long kMinChunk = 64;
-// Shared-memory budget for the per-slot partial means of one feature tile.
-constexpr int kInnerBudgetBytes = 24 * 1024;
-constexpr int kMaxSmemBytes = 227 * 1024;
+// Float4 stores per thread of the zero fill.  A flat grid of short CTAs that
+// each write one contiguous 16 KB block sustained ~7.4 TB/s on B200, ~18 %
+// more than grid-stride loops over the same buffer.
+constexpr int kFillVecsPerThread = 4;
 constexpr int64_t kMaxGrid = int64_t{1} << 20;
 
 std::atomic<uint64_t> g_launches{0};
@@ -64,47 +62,106 @@ __device__ __forceinline__ void flag_status(unsigned int bits) {
   atomicOr(&g_status, bits);
 }
 
-// T^n s: one nibble-table product per set bit of n.
-__device__ __forceinline__ uint64_t jump_ahead(uint64_t s, uint32_t n) {
-#pragma unroll 1
-  while (n != 0) {
-    const int j = __ffs(n) - 1;
-    n &= n - 1;
-    const uint64_t* tab = &g_jump.v[j][0][0];
-    uint64_t acc = 0;
+__device__ constexpr fsa::LaneTables g_lanes1 = fsa::make_lane_tables(fsa::kChunkLog2);
+__device__ constexpr fsa::LaneTables g_lanes2 = fsa::make_lane_tables(fsa::kChunkLog2 + 5);
+
+constexpr uint32_t kChunk = 1u << fsa::kChunkLog2;
+constexpr uint32_t kStarMulLo = static_cast<uint32_t>(fsa::kStarMul);
+constexpr uint32_t kStarMulHi = static_cast<uint32_t>(fsa::kStarMul >> 32);
+
+__device__ __forceinline__ uint64_t apply_table(const uint64_t* tab, uint64_t s) {
+  uint64_t acc = 0;
 #pragma unroll
-    for (int p = 0; p < 16; ++p) {
-      acc ^= __ldg(tab + p * 16 + static_cast<int>((s >> (4 * p)) & 15));
-    }
-    s = acc;
+  for (int p = 0; p < 16; ++p) {
+    acc ^= __ldg(tab + p * 16 + static_cast<int>((s >> (4 * p)) & 15));
+  }
+  return acc;
+}
+
+// State before the first draw of chunk j of a row whose initial state is s0,
+// i.e. T^(j * kChunk) s0 (see LaneTables in fsa_rng.cuh).
+__device__ __forceinline__ uint64_t chunk_start(uint64_t s0, uint32_t j) {
+  uint64_t s = apply_table(&g_lanes1.v[j & 31][0][0], s0);
+  if ((j >> 5) & 31) s = apply_table(&g_lanes2.v[(j >> 5) & 31][0][0], s);
+  uint32_t hi = j >> 10;
+#pragma unroll 1
+  while (hi != 0) {
+    const int b = __ffs(hi) - 1;
+    hi &= hi - 1;
+    s = apply_table(&g_jump.v[fsa::kChunkLog2 + 10 + b][0][0], s);
   }
   return s;
 }
 
-// Draws [t_begin, t_end) of one row whose reservoir holds `take` slots.
-// Draw t is row position take + t, uses the state after t + 1 steps and the
-// bound take + t + 1; a hit records position take + t in win[slot].
-__device__ __forceinline__ void run_draws(uint64_t s0, uint32_t t_begin,
-                                          uint32_t t_end, int take, int* win) {
-  uint64_t s = jump_ahead(s0, t_begin);
-  const uint32_t utake = static_cast<uint32_t>(take);
-#pragma unroll 2
-  for (uint32_t t = t_begin; t < t_end; ++t) {
+// Resolves one candidate draw exactly and records a hit.
+__device__ __forceinline__ void draw_hit(uint32_t lo, uint32_t r_hi, uint32_t bound,
+                                         uint32_t take, int* win) {
+  const uint64_t r = (static_cast<uint64_t>(r_hi) << 32) | (lo * kStarMulLo);
+  const uint32_t slot = fsa::bounded_draw(r, bound);
+  if (slot < take) atomicMax(&win[slot], static_cast<int>(bound - 1u));
+}
+
+// A draw with bound >= b_min can only hit (slot < take) if the high word of
+// r is below floor(take * 2^32 / b_min) + 1; the double quotient is exact to
+// within one unit, so +2 keeps the threshold conservative.
+__device__ __forceinline__ uint32_t hit_threshold(uint32_t take, uint32_t b_min) {
+  const double q = static_cast<double>(take) * 4294967296.0 / static_cast<double>(b_min);
+  return q >= 4294967293.0 ? 0xffffffffU : static_cast<uint32_t>(q) + 2u;
+}
+
+constexpr int kDrawGroup = 4;
+
+// `count` consecutive draws of one row starting at row position `pos`
+// (>= take) from state s: draw at position p steps the state, forms
+// r = state * M and selects slot floor(r * (p+1) / 2^64) if it is < take;
+// a hit records p in win[slot] (the largest hit position wins, which is the
+// last write of the reference's serial loop, fused_sample_agg.cu:47-52).
+// Only r's high word is formed per draw; groups of draws share one branch on
+// their smallest high word against the chunk's hit threshold.
+__device__ __forceinline__ void chunk_draws(uint64_t s, uint32_t pos, uint32_t count,
+                                            uint32_t take, int* win) {
+  uint32_t bound = pos + 1u;
+  const uint32_t thr = hit_threshold(take, bound);
+  uint32_t k = 0;
+  for (; k + kDrawGroup <= count; k += kDrawGroup, bound += kDrawGroup) {
+    uint32_t l[kDrawGroup], rh[kDrawGroup];
+    uint32_t rmin = 0xffffffffU;
+#pragma unroll
+    for (int u = 0; u < kDrawGroup; ++u) {
+      s = fsa::xorshift_step(s);
+      l[u] = static_cast<uint32_t>(s);
+      rh[u] = __umulhi(l[u], kStarMulLo) + l[u] * kStarMulHi +
+              static_cast<uint32_t>(s >> 32) * kStarMulLo;
+      rmin = min(rmin, rh[u]);
+    }
+    if (rmin < thr) {
+#pragma unroll
+      for (int u = 0; u < kDrawGroup; ++u) draw_hit(l[u], rh[u], bound + u, take, win);
+    }
+  }
+  for (; k < count; ++k, ++bound) {
     s = fsa::xorshift_step(s);
-    const uint32_t slot = fsa::bounded_draw(s * fsa::kStarMul, utake + t + 1u);
-    if (slot < utake) atomicMax(&win[slot], static_cast<int>(utake + t));
+    const uint32_t lo = static_cast<uint32_t>(s);
+    const uint32_t rh = __umulhi(lo, kStarMulLo) + lo * kStarMulHi +
+                        static_cast<uint32_t>(s >> 32) * kStarMulLo;
+    if (rh < thr) draw_hit(lo, rh, bound, take, win);
   }
 }
 
-// Splits the `ndraws` draws of a single row over the CTA.
-__device__ __forceinline__ void block_draws_one_row(uint64_t s0, int take,
-                                                    long long ndraws, int* win) {
-  const long long per = (ndraws + blockDim.x - 1) / blockDim.x;
-  const long long chunk = per > kMinChunk ? per : kMinChunk;
-  const long long g0 = static_cast<long long>(threadIdx.x) * chunk;
-  if (g0 >= ndraws) return;
-  const long long g1 = g0 + chunk < ndraws ? g0 + chunk : ndraws;
-  run_draws(s0, static_cast<uint32_t>(g0), static_cast<uint32_t>(g1), take, win);
+// Chunk j of a row with `take` slots and `ndraws` draws.
+__device__ __forceinline__ void row_chunk(uint64_t s0, uint32_t take, uint32_t ndraws,
+                                          uint32_t j, int* win) {
+  const uint32_t off = j * kChunk;
+  const uint32_t count = ndraws - off < kChunk ? ndraws - off : kChunk;
+  chunk_draws(chunk_start(s0, j), take + off, count, take, win);
+}
+
+// All draws of a single row, chunks spread over the CTA's threads.
+__device__ __forceinline__ void block_row_draws(uint64_t s0, int take, int ndraws, int* win) {
+  const uint32_t chunks = (static_cast<uint32_t>(ndraws) + kChunk - 1) / kChunk;
+  for (uint32_t j = threadIdx.x; j < chunks; j += blockDim.x) {
+    row_chunk(s0, static_cast<uint32_t>(take), static_cast<uint32_t>(ndraws), j, win);
+  }
 }
 
 // Reads row r of the CSR with validation.  Returns false (and flags) when the
@@ -246,7 +303,7 @@ __global__ void __launch_bounds__(kThreads1Hop)
     if (degree > take) {
       const uint64_t s0 = fsa::row_state(a.seed, static_cast<uint64_t>(root), 0,
                                          static_cast<uint64_t>(b + a.batch_offset));
-      block_draws_one_row(s0, take, static_cast<long long>(degree - take), slots);
+      block_row_draws(s0, take, degree - take, slots);
     }
     __syncthreads();
     for (int i = tid; i < k; i += nthreads) {
@@ -286,72 +343,64 @@ __global__ void __launch_bounds__(kThreads1Hop)
 
 // ---------------------------------------------------------------------------
 // 2-hop forward: fuseop/fused_sample_agg.cu:134-214
+//
+// The reference gives each root one CTA whose thread 0 runs the first-hop
+// reservoir and then all fanout1 second-hop reservoirs serially
+// (fused_sample_agg.cu:151-187).  Second-hop rows are size-biased (hubs), so
+// the work per root varies by orders of magnitude.  Here the forward is four
+// launches on the caller's stream:
+//
+//   plan   CTA per root: first-hop reservoir (draws split over the CTA),
+//          first-hop ids, and the table of second-hop rows (begin, take,
+//          draw count); second-hop winner slots set to -1.
+//   scan   one CTA: exclusive prefix of the draw counts of all B*fanout1
+//          second-hop rows -- the global draw space.
+//   draws  persistent grid: every thread takes an equal contiguous chunk of
+//          the global draw space, whichever rows and roots it spans, jumps
+//          to its first state and records winners with atomicMax.
+//   gather CTA per root: winners -> ids (col lookups), nested mean.
 // ---------------------------------------------------------------------------
 
-struct Fwd2Args {
+constexpr int kThreadsPlan = 128;
+constexpr int kThreadsScan = 1024;
+constexpr int kThreadsDraw = 256;
+constexpr int kThreadsGather = 256;
+
+struct Plan2Args {
   const int32_t* rowptr;
   const int32_t* col;
-  const float* x;
   int64_t num_nodes;
   int64_t num_edges;
-  int64_t feature_dim;
   const int32_t* frontier;
   int64_t batch_size;
   int64_t batch_offset;
   int fanout1;
   int fanout2;
   uint64_t seed;
-  float* out;
-  int32_t* samples1;
-  int32_t* samples2;
-  int dchunk;  // feature tile width (multiple of the vector width)
+  int32_t* s1;               // [B][k1] first-hop ids
+  int32_t* win2;             // [B][k1][k2] second-hop winners, -1 = slot kept
+  int32_t* mbeg;             // [R = B*k1] begin of each second-hop row
+  int32_t* mtake;            // [R] reservoir size of each second-hop row
+  int32_t* mdraws;           // [R] draws of each second-hop row
+  int32_t* nchunks;          // [R] kChunk-draw chunks of each second-hop row
+  unsigned long long* state; // [R] initial xorshift state of each second-hop row
+  unsigned int* done;        // [B] gather-kernel slot counters, reset here
+  unsigned long long* next;  // draw-kernel work counter, reset here
 };
 
-// Shared-memory layout of the 2-hop forward kernel, in bytes.
-struct Layout2 {
-  int pre, inner, s1, mbeg, mtake, mvalid, s2, misc, total;
-};
-
-__host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
-
-__host__ __device__ inline Layout2 layout_2hop(int k1, int k2, int dchunk) {
-  Layout2 l;
-  l.pre = 0;                                    // int64 [k1 + 1]
-  l.inner = align16(l.pre + 8 * (k1 + 1));      // float [k1][dchunk]
-  l.s1 = align16(l.inner + 4 * k1 * dchunk);    // int32 [k1]
-  l.mbeg = l.s1 + 4 * k1;                       // int32 [k1]
-  l.mtake = l.mbeg + 4 * k1;                    // int32 [k1]
-  l.mvalid = l.mtake + 4 * k1;                  // int32 [k1]
-  l.s2 = l.mvalid + 4 * k1;                     // int32 [k1 * k2]
-  l.misc = align16(l.s2 + 4 * k1 * k2);         // int32 [4]
-  l.total = l.misc + 16;
-  return l;
-}
-
-template <int V>
-__global__ void __launch_bounds__(kThreads2Hop)
-    fsa_2hop_forward_kernel(const Fwd2Args a) {
+__global__ void __launch_bounds__(kThreadsPlan)
+    fsa_2hop_plan_kernel(const Plan2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  int* s1 = reinterpret_cast<int*>(smem_raw);  // [k1] winners, then ids
   const int k1 = a.fanout1;
   const int k2 = a.fanout2;
-  const Layout2 L = layout_2hop(k1, k2, a.dchunk);
-  long long* pre = reinterpret_cast<long long*>(smem_raw + L.pre);
-  float* inner = reinterpret_cast<float*>(smem_raw + L.inner);
-  int* s1 = reinterpret_cast<int*>(smem_raw + L.s1);
-  int* mbeg = reinterpret_cast<int*>(smem_raw + L.mbeg);
-  int* mtake = reinterpret_cast<int*>(smem_raw + L.mtake);
-  int* mvalid = reinterpret_cast<int*>(smem_raw + L.mvalid);
-  int* s2 = reinterpret_cast<int*>(smem_raw + L.s2);
-  int* misc = reinterpret_cast<int*>(smem_raw + L.misc);
-
+  const int64_t k12 = static_cast<int64_t>(k1) * k2;
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
-  const int k12 = k1 * k2;
-  const int64_t D = a.feature_dim;
   const int64_t N = a.num_nodes;
+  if (blockIdx.x == 0 && tid == 0) *a.next = 0;
 
   for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
-    // ---- first hop: reservoir over row(root) -------------------------------
     const int32_t root = a.frontier[b];
     int32_t rbegin = 0, rdegree = 0;
     if (root >= 0 && root < N) {
@@ -363,25 +412,22 @@ __global__ void __launch_bounds__(kThreads2Hop)
     }
     const int take1 = rdegree < k1 ? rdegree : k1;
     for (int i = tid; i < k1; i += nthreads) s1[i] = -1;
-    for (int e = tid; e < k12; e += nthreads) s2[e] = -1;
-    if (tid == 0) misc[0] = 0;
+    for (int64_t e = tid; e < k12; e += nthreads) a.win2[b * k12 + e] = -1;
+    if (tid == 0) a.done[b] = 0;
     __syncthreads();
     if (rdegree > take1) {
       const uint64_t s0 = fsa::row_state(a.seed, static_cast<uint64_t>(root), 0,
                                          static_cast<uint64_t>(b + a.batch_offset));
-      block_draws_one_row(s0, take1, static_cast<long long>(rdegree - take1), s1);
+      block_row_draws(s0, take1, rdegree - take1, s1);
     }
     __syncthreads();
-
-    // ---- resolve first hop; read the middle rows ---------------------------
     for (int i = tid; i < k1; i += nthreads) {
       int32_t m = -1;
       if (i < take1) {
         const int w = s1[i];
         m = a.col[static_cast<int64_t>(rbegin) + (w >= 0 ? w : i)];
       }
-      s1[i] = m;
-      if (a.samples1 != nullptr) a.samples1[b * k1 + i] = m;
+      a.s1[b * k1 + i] = m;
       int32_t mb = 0, md = 0;
       if (m >= 0) {
         if (m < N) {
@@ -391,141 +437,272 @@ __global__ void __launch_bounds__(kThreads2Hop)
         }
       }
       const int mt = md < k2 ? md : k2;
-      mbeg[i] = mb;
-      mtake[i] = mt;
-      pre[i + 1] = static_cast<long long>(md - mt);
+      const int64_t r = b * k1 + i;
+      a.mbeg[r] = mb;
+      a.mtake[r] = mt;
+      a.mdraws[r] = md - mt;
+      a.nchunks[r] = static_cast<int32_t>((static_cast<uint32_t>(md - mt) + kChunk - 1) / kChunk);
+      a.state[r] = fsa::row_state(a.seed, static_cast<uint64_t>(root), 1, static_cast<uint64_t>(i));
     }
     __syncthreads();
+  }
+}
 
-    // ---- inclusive scan of per-row draw counts (warp 0) --------------------
-    if (tid < 32) {
-      const int seg = (k1 + 31) / 32;
-      const int i0 = min(tid * seg, k1);
-      const int i1 = min(i0 + seg, k1);
-      long long local = 0;
-      for (int i = i0; i < i1; ++i) local += pre[i + 1];
-      long long incl = local;
+struct Scan2Args {
+  const int32_t* nchunks;  // [R]
+  long long* pre;          // [R + 1] exclusive prefix, pre[R] = total chunks
+  int64_t rows;
+};
+
+constexpr int kScanItems = 4;
+
+// One CTA, tiles of blockDim * kScanItems rows: each thread scans its
+// contiguous items, warp shuffles and the warp totals give the tile prefix,
+// a running carry joins the tiles.
+__global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2Args a) {
+  __shared__ long long warp_sums[kThreadsScan / 32];
+  __shared__ long long carry;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nw = blockDim.x >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  const int64_t tile = static_cast<int64_t>(blockDim.x) * kScanItems;
+  for (int64_t t0 = 0; t0 < a.rows; t0 += tile) {
+    const int64_t i0 = t0 + static_cast<int64_t>(tid) * kScanItems;
+    long long v[kScanItems];
+    long long local = 0;
+#pragma unroll
+    for (int u = 0; u < kScanItems; ++u) {
+      v[u] = i0 + u < a.rows ? a.nchunks[i0 + u] : 0;
+      local += v[u];
+    }
+    long long incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffU, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      long long w = lane < nw ? warp_sums[lane] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const long long y = __shfl_up_sync(0xffffffffU, incl, o);
-        if (tid >= o) incl += y;
+        const long long y = __shfl_up_sync(0xffffffffU, w, o);
+        if (lane >= o) w += y;
       }
-      long long run = incl - local;
-      for (int i = i0; i < i1; ++i) {
-        run += pre[i + 1];
-        pre[i + 1] = run;
-      }
-      if (tid == 0) pre[0] = 0;
+      if (lane < nw) warp_sums[lane] = w;
     }
     __syncthreads();
-
-    // ---- second hop: the CTA splits the concatenated draws of all rows -----
-    const long long total = pre[k1];
-    if (total > 0) {
-      const long long per = (total + nthreads - 1) / nthreads;
-      const long long chunk = per > kMinChunk ? per : kMinChunk;
-      long long g = static_cast<long long>(tid) * chunk;
-      if (g < total) {
-        const long long gend = g + chunk < total ? g + chunk : total;
-        // Largest r with pre[r] <= g (rows with zero draws are skipped).
-        int lo = 0, hi = k1 - 1;
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (pre[mid] <= g) lo = mid; else hi = mid - 1;
-        }
-        int r = lo;
-        while (g < gend) {
-          while (pre[r + 1] <= g) ++r;
-          const long long row_end = pre[r + 1];
-          const long long seg_end = row_end < gend ? row_end : gend;
-          const uint64_t s0 = fsa::row_state(a.seed, static_cast<uint64_t>(root), 1,
-                                             static_cast<uint64_t>(r));
-          run_draws(s0, static_cast<uint32_t>(g - pre[r]),
-                    static_cast<uint32_t>(seg_end - pre[r]), mtake[r], s2 + r * k2);
-          g = seg_end;
-        }
-      }
-    }
-    __syncthreads();
-
-    // ---- resolve second hop -------------------------------------------------
-    for (int e = tid; e < k12; e += nthreads) {
-      const int i = e / k2;
-      const int j = e - i * k2;
-      int32_t id = -1;
-      if (j < mtake[i]) {
-        const int w = s2[e];
-        id = a.col[static_cast<int64_t>(mbeg[i]) + (w >= 0 ? w : j)];
-      }
-      s2[e] = id;
-      if (a.samples2 != nullptr) a.samples2[b * k12 + e] = id;
-    }
-    __syncthreads();
-    for (int i = tid; i < k1; i += nthreads) {
-      int valid = 0;
-      for (int j = 0; j < k2; ++j) {
-        const int32_t leaf = s2[i * k2 + j];
-        if (leaf >= 0) {
-          if (leaf < N) ++valid; else flag_status(FSA_STATUS_BAD_NEIGHBOR);
-        }
-      }
-      mvalid[i] = valid;
-      if (valid > 0) atomicAdd(&misc[0], 1);
-    }
-    __syncthreads();
-
-    // ---- nested mean, one feature tile at a time ----------------------------
-    const int nonempty = misc[0];
-    for (int64_t f0 = 0; f0 < D; f0 += a.dchunk) {
-      const int fc = static_cast<int>(D - f0 < a.dchunk ? D - f0 : a.dchunk);
-      const int nv = fc / V;
-      const int items = k1 * nv;
-      for (int it = tid; it < items; it += nthreads) {
-        const int i = it / nv;
-        const int v = it - i * nv;
-        const int valid = mvalid[i];
-        if (valid == 0) continue;
-        const int32_t* leaves = s2 + i * k2;
-        const float* base = a.x + f0 + v * V;
-        VecF<V> acc;
-        vzero(acc);
-#pragma unroll 4
-        for (int j = 0; j < k2; ++j) {
-          const int32_t leaf = leaves[j];
-          if (leaf >= 0 && leaf < N) {
-            const VecF<V> r = load_stream<V>(base + static_cast<int64_t>(leaf) * D);
+    long long run = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - local;
 #pragma unroll
-            for (int c = 0; c < V; ++c) acc.v[c] += r.v[c];
-          }
-        }
-        const float denom = static_cast<float>(valid);
+    for (int u = 0; u < kScanItems; ++u) {
+      if (i0 + u < a.rows) a.pre[i0 + u] = run;
+      run += v[u];
+    }
+    __syncthreads();
+    if (tid == 0) carry += warp_sums[nw - 1];
+    __syncthreads();
+  }
+  if (tid == 0) a.pre[a.rows] = carry;
+}
+
+struct Draw2Args {
+  const long long* pre;              // [R + 1] chunk prefix over second-hop rows
+  const unsigned long long* state;   // [R]
+  const int32_t* mtake;              // [R]
+  const int32_t* mdraws;             // [R]
+  int64_t rows;                      // R = B * k1
+  int fanout2;
+  int32_t* win2;                     // [R][k2]
+  unsigned long long* next;          // work counter (chunks handed out so far)
+};
+
+// Largest r in [lo, hi] with pre[r] <= q (pre[lo] <= q holds).
+__device__ __forceinline__ int64_t row_of(const long long* pre, int64_t lo, int64_t hi,
+                                          long long q) {
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (__ldg(pre + mid) <= q) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Persistent grid; each warp repeatedly takes the next 32 chunks of the
+// global chunk sequence (second-hop rows in (root, slot) order, each row's
+// chunks in position order), one chunk per lane.  Lane 0 binary-searches the
+// row of the first chunk; the other lanes find theirs among the next 32 row
+// boundaries with a shuffle search.
+__global__ void __launch_bounds__(kThreadsDraw) fsa_2hop_draw_kernel(const Draw2Args a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t R = a.rows;
+  const long long total = __ldg(a.pre + R);
+  while (true) {
+    unsigned long long base = 0;
+    if (lane == 0) base = atomicAdd(a.next, 32ULL);
+    base = __shfl_sync(0xffffffffU, base, 0);
+    if (static_cast<long long>(base) >= total) break;
+    const long long q0 = static_cast<long long>(base);
+    const long long q = q0 + lane;
+    int64_t r0 = 0;
+    if (lane == 0) r0 = row_of(a.pre, 0, R - 1, q0);
+    r0 = __shfl_sync(0xffffffffU, r0, 0);
+    // e = pre[r0 + 1 + lane]; this lane's row is r0 + #{m : e_m <= q}.
+    const int64_t ei = r0 + 1 + lane;
+    const long long e = ei <= R ? __ldg(a.pre + ei) : LLONG_MAX;
+    int c = 0;
+#pragma unroll
+    for (int step = 16; step > 0; step >>= 1) {
+      const long long em = __shfl_sync(0xffffffffU, e, c + step - 1);
+      if (em <= q) c += step;
+    }
+    // Every lane takes part in the shuffle (a full-mask shuffle reached by
+    // only some lanes never completes).
+    const long long e_last = __shfl_sync(0xffffffffU, e, 31);
+    if (c == 31 && e_last <= q) c = 32;
+    if (q >= total) continue;
+    int64_t r = r0 + c;
+    if (c == 32) r = row_of(a.pre, r0 + 32, R - 1, q);  // > 32 row boundaries in 32 chunks
+    const uint32_t j = static_cast<uint32_t>(q - __ldg(a.pre + r));
+    row_chunk(__ldg(a.state + r), static_cast<uint32_t>(__ldg(a.mtake + r)),
+              static_cast<uint32_t>(__ldg(a.mdraws + r)), j, a.win2 + r * a.fanout2);
+  }
+}
+
+struct Gather2Args {
+  const int32_t* col;
+  const float* x;
+  int64_t num_nodes;
+  int64_t feature_dim;
+  int64_t batch_size;
+  int fanout1;
+  int fanout2;
+  const int32_t* mbeg;
+  const int32_t* mtake;
+  int32_t* win2;       // [B][k1][k2] winners in, second-hop ids out (in place)
+  float* inner;        // [B][k1][D] slot means (workspace)
+  int32_t* mvalid;     // [B][k1] valid leaves per slot (workspace)
+  unsigned int* done;  // [B] slots finished per root, zeroed by the plan kernel
+  float* out;
+};
+
+// Rows gathered per batch of independent loads (per lane).
+constexpr int kGatherBatch = 8;
+
+// Inner sum of one (slot, feature vector): valid leaves in j order from 0.0f.
+template <int V>
+__device__ __forceinline__ VecF<V> leaf_sum(const int32_t* leaves, int k2, const float* base,
+                                            int64_t D, int64_t N) {
+  VecF<V> acc;
+  vzero(acc);
+  for (int j0 = 0; j0 < k2; j0 += kGatherBatch) {
+    VecF<V> r[kGatherBatch];
+    bool ok[kGatherBatch];
+#pragma unroll
+    for (int u = 0; u < kGatherBatch; ++u) {
+      const int32_t leaf = j0 + u < k2 ? leaves[j0 + u] : -1;
+      ok[u] = leaf >= 0 && leaf < N;
+      if (ok[u]) r[u] = load_stream<V>(base + static_cast<int64_t>(leaf) * D);
+    }
+#pragma unroll
+    for (int u = 0; u < kGatherBatch; ++u) {
+      if (ok[u]) {
+#pragma unroll
+        for (int c = 0; c < V; ++c) acc.v[c] += r[u].v[c];
+      }
+    }
+  }
+  return acc;
+}
+
+// One warp per (root, first-hop slot), no CTA barriers.  The warp resolves
+// the slot's winners to leaf ids (written back in place: they are the
+// saved samples2 when requested), gathers the leaf rows and writes the slot
+// mean (inner sum over j in order / valid) to a scratch row.  The last warp
+// to finish a root -- device-scope fence, then a counter; nothing waits --
+// sums the slot means in slot order and divides by the non-empty count
+// (fused_sample_agg.cu:189-213), so outputs keep the reference's bits.
+template <int V>
+__global__ void __launch_bounds__(kThreadsGather, 4)
+    fsa_2hop_gather_kernel(const Gather2Args a) {
+  const int lane = threadIdx.x & 31;
+  const int k1 = a.fanout1;
+  const int k2 = a.fanout2;
+  const int64_t k12 = static_cast<int64_t>(k1) * k2;
+  const int64_t D = a.feature_dim;
+  const int64_t N = a.num_nodes;
+  const int64_t nv = D / V;
+  const int64_t nslots = a.batch_size * k1;
+  const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       w < nslots; w += wstride) {
+    const int64_t b = w / k1;
+    const int i = static_cast<int>(w - b * k1);
+    // ---- winners -> leaf ids (the serial loop's final reservoir) ----------
+    const int t = __ldg(a.mtake + w);
+    const int mb = __ldg(a.mbeg + w);
+    int32_t* leaves = a.win2 + b * k12 + static_cast<int64_t>(i) * k2;
+    int valid = 0;
+    for (int j = lane; j < k2; j += 32) {
+      int32_t id = -1;
+      if (j < t) {
+        const int win = leaves[j];
+        id = __ldg(a.col + static_cast<int64_t>(mb) + (win >= 0 ? win : j));
+      }
+      leaves[j] = id;
+      if (id >= 0) {
+        if (id < N) ++valid; else flag_status(FSA_STATUS_BAD_NEIGHBOR);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) valid += __shfl_xor_sync(0xffffffffU, valid, o);
+    __syncwarp();
+    // ---- slot mean --------------------------------------------------------
+    float* slot_mean = a.inner + w * D;
+    if (valid > 0) {
+      const float denom = static_cast<float>(valid);
+      for (int64_t v = lane; v < nv; v += 32) {
+        VecF<V> acc = leaf_sum<V>(leaves, k2, a.x + v * V, D, N);
 #pragma unroll
         for (int c = 0; c < V; ++c) acc.v[c] = acc.v[c] / denom;
-        store_vec(inner + i * a.dchunk + v * V, acc);
+        store_vec(slot_mean + v * V, acc);
       }
-      __syncthreads();
-      for (int v = tid; v < nv; v += nthreads) {
-        VecF<V> outer;
-        vzero(outer);
-        for (int i = 0; i < k1; ++i) {
-          if (mvalid[i] > 0) {
-            const VecF<V> m = load_vec<V>(inner + i * a.dchunk + v * V);
-#pragma unroll
-            for (int c = 0; c < V; ++c) outer.v[c] += m.v[c];
-          }
-        }
-        if (nonempty > 0) {
-          const float denom = static_cast<float>(nonempty);
-#pragma unroll
-          for (int c = 0; c < V; ++c) outer.v[c] = outer.v[c] / denom;
-        } else {
-          vzero(outer);
-        }
-        store_vec(a.out + b * D + f0 + v * V, outer);
-      }
-      __syncthreads();
     }
-    __syncthreads();
+    if (lane == 0) a.mvalid[w] = valid;
+    __threadfence();
+    __syncwarp();
+    unsigned int prev = 0;
+    if (lane == 0) prev = atomicAdd(a.done + b, 1u);
+    prev = __shfl_sync(0xffffffffU, prev, 0);
+    if (prev != static_cast<unsigned int>(k1 - 1)) continue;
+    // ---- last slot of root b: ordered sum of the slot means ---------------
+    __threadfence();
+    const int32_t* mv = a.mvalid + b * k1;
+    int nonempty = 0;
+    for (int s = lane; s < k1; s += 32) nonempty += __ldcg(mv + s) > 0 ? 1 : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) nonempty += __shfl_xor_sync(0xffffffffU, nonempty, o);
+    const float* means = a.inner + b * k1 * D;
+    for (int64_t v = lane; v < nv; v += 32) {
+      VecF<V> outer;
+      vzero(outer);
+      for (int s = 0; s < k1; ++s) {
+        if (__ldcg(mv + s) > 0) {
+#pragma unroll
+          for (int c = 0; c < V; ++c) outer.v[c] += __ldcg(means + s * D + v * V + c);
+        }
+      }
+      if (nonempty > 0) {
+        const float denom = static_cast<float>(nonempty);
+#pragma unroll
+        for (int c = 0; c < V; ++c) outer.v[c] = outer.v[c] / denom;
+      } else {
+        vzero(outer);
+      }
+      store_vec(a.out + b * D + v * V, outer);
+    }
   }
 }
 
@@ -649,15 +826,22 @@ __global__ void __launch_bounds__(kThreadsBwd)
 
 __global__ void __launch_bounds__(kThreadsFill)
     fsa_fill_zero_kernel(float* __restrict__ dst, int64_t count) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n4 = count >> 2;
+  const int64_t base =
+      static_cast<int64_t>(blockIdx.x) * blockDim.x * kFillVecsPerThread + threadIdx.x;
   float4* d4 = reinterpret_cast<float4*>(dst);
-  for (int64_t i = t0; i < n4; i += stride) {
-    asm volatile("st.global.cs.v4.f32 [%0], {%1,%1,%1,%1};" ::"l"(d4 + i), "f"(0.0F)
-                 : "memory");
+#pragma unroll
+  for (int k = 0; k < kFillVecsPerThread; ++k) {
+    const int64_t i = base + static_cast<int64_t>(k) * blockDim.x;
+    if (i < n4) {
+      asm volatile("st.global.cs.v4.f32 [%0], {%1,%1,%1,%1};" ::"l"(d4 + i), "f"(0.0F)
+                   : "memory");
+    }
   }
-  for (int64_t i = (n4 << 2) + t0; i < count; i += stride) dst[i] = 0.0F;
+  // The count % 4 tail, by the first threads of the last CTA.
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x < (count & 3)) {
+    dst[(n4 << 2) + threadIdx.x] = 0.0F;
+  }
 }
 
 __global__ void __launch_bounds__(kThreadsFill)
@@ -713,20 +897,69 @@ int launch(Kernel kernel, int grid, int block, int smem, cudaStream_t stream,
   return check_launch();
 }
 
-// Tile width and vector width of the 2-hop forward that fit shared memory.
-bool plan_2hop(int k1, int k2, int64_t D, int vec, int* dchunk_out, int* smem_out) {
-  int dchunk = 0;
-  if (D > 0) {
-    const int64_t fit = kInnerBudgetBytes / (4 * static_cast<int64_t>(k1));
-    int64_t c = fit < D ? fit : D;
-    c -= c % vec;
-    if (c < vec) c = vec;
-    dchunk = static_cast<int>(c);
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+// Workspace of the 2-hop forward, in bytes from a 256-byte aligned base.
+struct Ws2 {
+  size_t pre, state, nchunks, mbeg, mtake, mdraws, next, done, mvalid, inner, s1, win2, total;
+};
+
+Ws2 ws2_layout(int64_t B, int k1, int k2, int64_t D, bool need_s1, bool need_win2) {
+  Ws2 l{};
+  const size_t rows = static_cast<size_t>(B) * static_cast<size_t>(k1);
+  size_t off = 0;
+  l.pre = off;
+  off = align256(off + 8 * (rows + 1));
+  l.state = off;
+  off = align256(off + 8 * rows);
+  l.nchunks = off;
+  off = align256(off + 4 * rows);
+  l.mbeg = off;
+  off = align256(off + 4 * rows);
+  l.mtake = off;
+  off = align256(off + 4 * rows);
+  l.mdraws = off;
+  off = align256(off + 4 * rows);
+  l.next = off;
+  off = align256(off + 8);
+  l.done = off;
+  off = align256(off + 4 * static_cast<size_t>(B));
+  l.mvalid = off;
+  off = align256(off + 4 * rows);
+  l.inner = off;
+  off = align256(off + 4 * rows * static_cast<size_t>(D));
+  l.s1 = off;
+  if (need_s1) off = align256(off + 4 * rows);
+  l.win2 = off;
+  if (need_win2) off = align256(off + 4 * rows * static_cast<size_t>(k2));
+  l.total = off;
+  return l;
+}
+
+// Persistent grid of the draw kernel.
+int draw_grid(int* grid_out) {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) {
+    *grid_out = cached[dev];
+    return FSA_OK;
   }
-  const Layout2 l = layout_2hop(k1, k2, dchunk);
-  *dchunk_out = dchunk;
-  *smem_out = l.total;
-  return l.total <= kMaxSmemBytes;
+  int sms = 0, per_sm = 0;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (err == cudaSuccess) {
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fsa_2hop_draw_kernel,
+                                                        kThreadsDraw, 0);
+  }
+  if (err != cudaSuccess) return cuda_fail(err);
+  // One CTA per SM below full occupancy: the warps grab work dynamically, so
+  // this costs no balance, and it leaves room for the gradient zero-fill,
+  // which the autograd path runs concurrently on another stream.
+  const int grid = sms * (per_sm > 1 ? per_sm - 1 : 1);
+  if (dev >= 0 && dev < 64) cached[dev] = grid;
+  *grid_out = grid;
+  return FSA_OK;
 }
 
 }  // namespace
@@ -789,6 +1022,14 @@ int fsa_sample_agg_backward(const int32_t* samples, const int32_t* takes,
   }
 }
 
+size_t fsa_sample_agg_2hop_workspace_size(int64_t batch_size, int32_t fanout1,
+                                          int32_t fanout2, int64_t feature_dim,
+                                          int has_samples1, int has_samples2) {
+  if (batch_size <= 0 || fanout1 <= 0 || fanout2 <= 0 || feature_dim < 0) return 0;
+  return ws2_layout(batch_size, fanout1, fanout2, feature_dim, has_samples1 == 0,
+                    has_samples2 == 0).total;
+}
+
 int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
                                 int64_t num_nodes, int64_t num_edges,
                                 const float* x, int64_t feature_dim,
@@ -796,6 +1037,7 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
                                 int64_t batch_offset, int32_t fanout1,
                                 int32_t fanout2, uint64_t seed, float* out,
                                 int32_t* samples1, int32_t* samples2,
+                                void* workspace, size_t workspace_bytes,
                                 void* stream) {
   if (fanout1 < 0 || fanout2 < 0 || batch_size < 0 || feature_dim < 0 ||
       num_nodes < 0 || num_edges < 0 || batch_offset < 0) {
@@ -810,21 +1052,50 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
       (feature_dim > 0 && (out == nullptr || (num_nodes > 0 && x == nullptr)))) {
     return FSA_ERR_INVALID_ARGUMENT;
   }
-  int vec = pick_vec(feature_dim, x, out);
-  int dchunk = 0, smem = 0;
-  while (!plan_2hop(fanout1, fanout2, feature_dim, vec, &dchunk, &smem)) {
-    if (vec == 1) return FSA_ERR_INVALID_ARGUMENT;
-    vec >>= 1;
+  const Ws2 wl = ws2_layout(batch_size, fanout1, fanout2, feature_dim, samples1 == nullptr,
+                            samples2 == nullptr);
+  if (workspace == nullptr || workspace_bytes < wl.total || !aligned(workspace, 256)) {
+    return FSA_ERR_INVALID_ARGUMENT;
   }
-  Fwd2Args a{rowptr, col, x, num_nodes, num_edges, feature_dim, frontier,
-             batch_size, batch_offset, fanout1, fanout2, seed, out, samples1,
-             samples2, dchunk};
-  const int grid = grid_for(batch_size);
+  const int vec = pick_vec(feature_dim, x, out);
+  char* ws = static_cast<char*>(workspace);
+  int32_t* s1 = samples1 != nullptr ? samples1 : reinterpret_cast<int32_t*>(ws + wl.s1);
+  int32_t* win2 = samples2 != nullptr ? samples2 : reinterpret_cast<int32_t*>(ws + wl.win2);
+  auto* pre = reinterpret_cast<long long*>(ws + wl.pre);
+  auto* state = reinterpret_cast<unsigned long long*>(ws + wl.state);
+  auto* nchunks = reinterpret_cast<int32_t*>(ws + wl.nchunks);
+  auto* mbeg = reinterpret_cast<int32_t*>(ws + wl.mbeg);
+  auto* mtake = reinterpret_cast<int32_t*>(ws + wl.mtake);
+  auto* mdraws = reinterpret_cast<int32_t*>(ws + wl.mdraws);
+  auto* next = reinterpret_cast<unsigned long long*>(ws + wl.next);
+  auto* done = reinterpret_cast<unsigned int*>(ws + wl.done);
+  auto* mvalid = reinterpret_cast<int32_t*>(ws + wl.mvalid);
+  auto* inner = reinterpret_cast<float*>(ws + wl.inner);
   auto s = static_cast<cudaStream_t>(stream);
+  const int64_t rows = batch_size * fanout1;
+
+  const Plan2Args pa{rowptr, col, num_nodes, num_edges, frontier, batch_size, batch_offset,
+                     fanout1, fanout2, seed, s1, win2, mbeg, mtake, mdraws, nchunks, state,
+                     done, next};
+  int st = launch(fsa_2hop_plan_kernel, grid_for(batch_size), kThreadsPlan, 4 * fanout1, s, pa);
+  if (st != FSA_OK) return st;
+  const Scan2Args sa{nchunks, pre, rows};
+  st = launch(fsa_2hop_scan_kernel, 1, kThreadsScan, 0, s, sa);
+  if (st != FSA_OK) return st;
+  int dgrid = 0;
+  st = draw_grid(&dgrid);
+  if (st != FSA_OK) return st;
+  const Draw2Args da{pre, state, mtake, mdraws, rows, fanout2, win2, next};
+  st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, 0, s, da);
+  if (st != FSA_OK) return st;
+  const Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
+                       mtake, win2, inner, mvalid, done, out};
+  const int64_t warps_per_cta = kThreadsGather / 32;
+  const int ggrid = grid_for((batch_size * fanout1 + warps_per_cta - 1) / warps_per_cta);
   switch (vec) {
-    case 4: return launch(fsa_2hop_forward_kernel<4>, grid, kThreads2Hop, smem, s, a);
-    case 2: return launch(fsa_2hop_forward_kernel<2>, grid, kThreads2Hop, smem, s, a);
-    default: return launch(fsa_2hop_forward_kernel<1>, grid, kThreads2Hop, smem, s, a);
+    case 4: return launch(fsa_2hop_gather_kernel<4>, ggrid, kThreadsGather, 0, s, ga);
+    case 2: return launch(fsa_2hop_gather_kernel<2>, ggrid, kThreadsGather, 0, s, ga);
+    default: return launch(fsa_2hop_gather_kernel<1>, ggrid, kThreadsGather, 0, s, ga);
   }
 }
 
@@ -862,19 +1133,21 @@ int fsa_sample_agg_2hop_backward(const float* grad_out, const int32_t* samples1,
 int fsa_fill_zero_f32(float* dst, int64_t count, void* stream) {
   if (count < 0 || (count > 0 && dst == nullptr)) return FSA_ERR_INVALID_ARGUMENT;
   if (count == 0) return FSA_OK;
-  int device = 0, sms = 0;
-  cudaError_t err = cudaGetDevice(&device);
-  if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  if (err != cudaSuccess) return cuda_fail(err);
-  // Enough CTAs for every SM to keep stores in flight; each thread loops.
-  const int64_t want = (count / 4 + kThreadsFill - 1) / kThreadsFill;
-  const int64_t cap = static_cast<int64_t>(sms) * 8;
-  const int grid = static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
   auto s = static_cast<cudaStream_t>(stream);
   if (aligned(dst, 16)) {
-    fsa_fill_zero_kernel<<<grid, kThreadsFill, 0, s>>>(dst, count);
+    const int64_t per_cta = static_cast<int64_t>(kThreadsFill) * kFillVecsPerThread;
+    const int64_t grid = ((count >> 2) + per_cta - 1) / per_cta;
+    if (grid > 0x7fffffff) return FSA_ERR_INVALID_ARGUMENT;
+    fsa_fill_zero_kernel<<<static_cast<unsigned int>(grid > 0 ? grid : 1), kThreadsFill, 0, s>>>(
+        dst, count);
   } else {
-    fsa_fill_zero_scalar_kernel<<<grid, kThreadsFill, 0, s>>>(dst, count);
+    int device = 0, sms = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err == cudaSuccess) {
+      err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    }
+    if (err != cudaSuccess) return cuda_fail(err);
+    fsa_fill_zero_scalar_kernel<<<sms * 8, kThreadsFill, 0, s>>>(dst, count);
   }
   return check_launch();
 }

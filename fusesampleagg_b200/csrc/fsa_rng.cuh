@@ -105,6 +105,51 @@ constexpr JumpTables make_jump_tables() {
   return t;
 }
 
+// Draws are handed out in chunks of 2^kChunkLog2 positions aligned to the
+// start of each row; a warp takes 32 consecutive chunks.  LaneTables holds
+// T^(l * 2^step_log2) for l < 32 in the same nibble form.  With one set for
+// step 2^kChunkLog2 (one chunk) and one for 32 chunks, the start state of
+// chunk j of a row is  K1[j % 32] * K2[(j / 32) % 32] * T^(...) s0: one or
+// two table products per lane, plus one jump matrix per set bit of j / 1024
+// (rows of more than 2^(kChunkLog2 + 10) draws only).
+constexpr int kChunkLog2 = 5;
+constexpr int kLaneTables = 32;
+
+struct LaneTables {
+  uint64_t v[kLaneTables][16][16];
+};
+
+constexpr uint64_t apply_nibbles(const uint64_t (&tab)[16][16], uint64_t s) {
+  uint64_t acc = 0;
+  for (int p = 0; p < 16; ++p) acc ^= tab[p][(s >> (4 * p)) & 15];
+  return acc;
+}
+
+constexpr LaneTables make_lane_tables(int step_log2) {
+  const JumpTables jt = make_jump_tables();
+  LaneTables t{};
+  // Identity for l = 0.
+  for (int p = 0; p < 16; ++p) {
+    for (int nib = 0; nib < 16; ++nib) t.v[0][p][nib] = static_cast<uint64_t>(nib) << (4 * p);
+  }
+  uint64_t step_cols[64] = {};  // columns of T^(2^step_log2)
+  for (int k = 0; k < 64; ++k) step_cols[k] = apply_nibbles(jt.v[step_log2], uint64_t{1} << k);
+  for (int l = 1; l < kLaneTables; ++l) {
+    uint64_t cols[64] = {};  // columns of T^(l * step) = T^((l-1) * step) * T^step
+    for (int k = 0; k < 64; ++k) cols[k] = apply_nibbles(t.v[l - 1], step_cols[k]);
+    for (int p = 0; p < 16; ++p) {
+      for (int nib = 0; nib < 16; ++nib) {
+        uint64_t acc = 0;
+        for (int b = 0; b < 4; ++b) {
+          if ((nib >> b) & 1) acc ^= cols[4 * p + b];
+        }
+        t.v[l][p][nib] = acc;
+      }
+    }
+  }
+  return t;
+}
+
 // Host-side evaluation of T^n s (tests and host tools).
 inline uint64_t jump_host(const JumpTables& t, uint64_t s, uint64_t n) {
   for (int j = 0; j < kJumpBits && n != 0; ++j, n >>= 1) {
@@ -115,6 +160,54 @@ inline uint64_t jump_host(const JumpTables& t, uint64_t s, uint64_t n) {
     }
   }
   return s;
+}
+
+// Host-side start state of chunk j of a row (the device uses the same
+// decomposition).
+inline uint64_t chunk_start_host(const JumpTables& jt, const LaneTables& k1,
+                                 const LaneTables& k2, uint64_t s0, uint64_t j) {
+  uint64_t s = apply_nibbles(k1.v[j % kLaneTables], s0);
+  s = apply_nibbles(k2.v[(j / kLaneTables) % kLaneTables], s);
+  uint64_t hi = j / (kLaneTables * kLaneTables);
+  for (int b = 0; hi != 0; ++b, hi >>= 1) {
+    if (hi & 1) s = apply_nibbles(jt.v[kChunkLog2 + 10 + b], s);
+  }
+  return s;
+}
+
+// Multipliers 2^20, 2^25 and 2^5, passed as kernel arguments so that the
+// compiler keeps the shifts below as integer multiplies (FMA pipe) instead
+// of turning them back into shift instructions (ALU pipe): the draw loop is
+// otherwise bound by the ALU pipe, which also executes every XOR.
+struct ShiftMultipliers {
+  uint32_t m20, m25, m5;
+};
+
+constexpr ShiftMultipliers kShiftMultipliers{1u << 20, 1u << 25, 1u << 5};
+
+FSA_HD uint32_t mulhi32(uint32_t a, uint32_t b) {
+#if defined(__CUDA_ARCH__)
+  return __umulhi(a, b);
+#else
+  return static_cast<uint32_t>((static_cast<uint64_t>(a) * b) >> 32);
+#endif
+}
+
+// One xorshift64 step on 32-bit halves:
+//   s >> 12: hi*2^20 gives (hi >> 12 : hi << 20); lo >> 12 = mulhi(lo, 2^20)
+//   s << 25: lo*2^25 gives (lo >> 7 : lo << 25);  hi << 25 = hi * 2^25
+//   s >> 27: hi*2^5  gives (hi >> 27 : hi << 5);  lo >> 27 = mulhi(lo, 2^5)
+// The two parts of each shifted half never overlap, so adding them is OR.
+FSA_HD void xorshift_step_mul(uint32_t& lo, uint32_t& hi, const ShiftMultipliers& m) {
+  uint64_t t = static_cast<uint64_t>(hi) * m.m20;
+  lo ^= mulhi32(lo, m.m20) + static_cast<uint32_t>(t);
+  hi ^= static_cast<uint32_t>(t >> 32);
+  t = static_cast<uint64_t>(lo) * m.m25;
+  hi ^= hi * m.m25 + static_cast<uint32_t>(t >> 32);
+  lo ^= static_cast<uint32_t>(t);
+  t = static_cast<uint64_t>(hi) * m.m5;
+  lo ^= mulhi32(lo, m.m5) + static_cast<uint32_t>(t);
+  hi ^= static_cast<uint32_t>(t >> 32);
 }
 
 }  // namespace fsa

@@ -49,8 +49,19 @@ class Graph:
         return h.hexdigest()
 
 
-def _generator(seed: int, device) -> torch.Generator:
-    return torch.Generator(device=torch.device(device)).manual_seed(int(seed))
+# Each generator mixes its purpose into the seed, so that e.g. graph seed 0
+# and root-batch seed 0 do not share a random stream (they would otherwise
+# draw the same permutation, making root batch 0 the graph's top hubs).
+_SALT = {"graph": 0x6772617068, "poisson": 0x706F6973, "features": 0x66656174,
+         "roots": 0x726F6F7473}
+
+
+def _generator(seed: int, device, purpose: str) -> torch.Generator:
+    v = (int(seed) * 0x9E3779B97F4A7C15 + _SALT[purpose]) & ((1 << 64) - 1)
+    v ^= v >> 31
+    v = (v * 0xBF58476D1CE4E5B9) & ((1 << 64) - 1)
+    v ^= v >> 29
+    return torch.Generator(device=torch.device(device)).manual_seed(v & ((1 << 63) - 1))
 
 
 def csr_from_edges(src: torch.Tensor, dst: torch.Tensor, num_nodes: int,
@@ -88,7 +99,7 @@ def poisson_graph(num_nodes: int, mean_degree: float, zero_fraction: float,
                   seed: int, device="cpu") -> Graph:
     """Uniform random directed graph: out-degree ~ Poisson(mean_degree),
     self-loops excluded, ``zero_fraction`` of the nodes forced to degree 0."""
-    g = _generator(seed, device)
+    g = _generator(seed, device, "poisson")
     deg = torch.poisson(torch.full((num_nodes,), float(mean_degree), device=device),
                         generator=g).to(torch.int64)
     n_zero = int(round(zero_fraction * num_nodes))
@@ -129,7 +140,7 @@ def chung_lu_graph(num_nodes: int, num_edges: int, exponent: float,
     that hubs are scattered over the id space.  ``oversample`` compensates
     for the duplicate pairs that hubs produce.
     """
-    g = _generator(seed, device)
+    g = _generator(seed, device, "graph")
     w = chung_lu_weights(num_nodes, num_edges, exponent, max_degree, device)
     cdf = torch.cumsum(w, 0)
     total = float(cdf[-1])
@@ -154,7 +165,7 @@ def chung_lu_graph(num_nodes: int, num_edges: int, exponent: float,
 
 
 def features(num_nodes: int, dim: int, seed: int, device="cpu", std: float = 1.0) -> torch.Tensor:
-    g = _generator(seed, device)
+    g = _generator(seed, device, "features")
     x = torch.randn(num_nodes, dim, generator=g, device=device, dtype=torch.float32)
     if std != 1.0:
         x.mul_(std)
@@ -163,7 +174,7 @@ def features(num_nodes: int, dim: int, seed: int, device="cpu", std: float = 1.0
 
 def root_batch(num_nodes: int, batch: int, seed: int, device="cpu") -> torch.Tensor:
     """``batch`` distinct uniformly drawn root ids (int32)."""
-    g = _generator(seed, device)
+    g = _generator(seed, device, "roots")
     if batch > num_nodes:
         raise ValueError("batch larger than the node count")
     if num_nodes <= 1 << 22:

@@ -17,12 +17,14 @@
  * Layouts: rowptr int32[num_nodes+1], col int32[num_edges] (CSR, neighbour
  * order within a row is significant), x float32[num_nodes][feature_dim]
  * row-major, frontier int32[batch_size].  All pointers are device pointers.
- * Calls are asynchronous and stream-ordered; nothing is allocated and the
+ * Calls are asynchronous and stream-ordered; nothing is allocated (scratch
+ * comes from a caller-provided workspace where a call needs one) and the
  * host is never synchronised (except fsa_device_status).
  */
 #ifndef FSA_SM100_H_
 #define FSA_SM100_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(FSA_BUILD_SHARED)
@@ -85,15 +87,27 @@ FSA_API int fsa_sample_agg_backward(const int32_t* samples, const int32_t* takes
  * second-hop slots j of x[samples2[b,i,j],:]).  samples1
  * int32[batch_size][fanout1] and samples2 int32[batch_size][fanout1][fanout2]
  * are optional (NULL = not written).
+ *
+ * Unlike the reference launcher this one needs a device workspace (the
+ * second-hop row table, chunk prefixes, per-slot means, plus the id
+ * buffers that are not requested as outputs): at least
+ * fsa_sample_agg_2hop_workspace_size(...) bytes, 256-byte aligned, owned by
+ * the caller and not used by anything else until the call's work on `stream`
+ * has finished.  Its contents need no initialisation.
  */
+FSA_API size_t fsa_sample_agg_2hop_workspace_size(int64_t batch_size, int32_t fanout1,
+                                                  int32_t fanout2, int64_t feature_dim,
+                                                  int has_samples1, int has_samples2);
+
 FSA_API int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
-                                int64_t num_nodes, int64_t num_edges,
-                                const float* x, int64_t feature_dim,
-                                const int32_t* frontier, int64_t batch_size,
-                                int64_t batch_offset, int32_t fanout1,
-                                int32_t fanout2, uint64_t seed, float* out,
-                                int32_t* samples1, int32_t* samples2,
-                                void* stream);
+                                        int64_t num_nodes, int64_t num_edges,
+                                        const float* x, int64_t feature_dim,
+                                        const int32_t* frontier, int64_t batch_size,
+                                        int64_t batch_offset, int32_t fanout1,
+                                        int32_t fanout2, uint64_t seed, float* out,
+                                        int32_t* samples1, int32_t* samples2,
+                                        void* workspace, size_t workspace_bytes,
+                                        void* stream);
 
 /*
  * 2-hop backward (saved-index replay).  Replaces

@@ -82,6 +82,11 @@ GRAPHS = {
 
 
 def frontier_for(graph_name: str, graph: synthetic.Graph, batch: int, seed: int) -> torch.Tensor:
+    """Roots of a case; ``seed == -1`` selects the ``batch`` highest-degree
+    nodes (hub roots: every first-hop row is long)."""
+    if seed == -1:
+        order = torch.sort(graph.degrees(), descending=True, stable=True).indices
+        return order[:batch].to(torch.int32)
     if graph_name == "toy":
         # Every node, the empty row included, and a repeated root.
         return torch.tensor([0, 3, 2, 6, 7, 1, 4, 5, 3], dtype=torch.int32)
@@ -117,6 +122,9 @@ CASES = [
     _c("powerlaw_2hop_8x4_s9", "powerlaw", 2, (8, 4), 9, 64, batch=256, root_seed=3),
     _c("powerlaw_1hop_k8_s1234", "powerlaw", 1, (8,), 1234, 100, batch=256, root_seed=4),
     _c("powerlaw_1hop_k100_s2", "powerlaw", 1, (100,), 2, 3, batch=128, root_seed=5),
+    # hub roots: long first-hop rows for every root
+    _c("powerlaw_2hop_15x10_hubroots", "powerlaw", 2, (15, 10), 11, 16, batch=128, root_seed=-1),
+    _c("powerlaw_1hop_k10_hubroots", "powerlaw", 1, (10,), 12, 16, batch=128, root_seed=-1),
 ]
 
 

@@ -7,6 +7,8 @@
 #include "fsa_rng.cuh"
 
 static const fsa::JumpTables kTables = fsa::make_jump_tables();
+static const fsa::LaneTables kLanes1 = fsa::make_lane_tables(fsa::kChunkLog2);
+static const fsa::LaneTables kLanes2 = fsa::make_lane_tables(fsa::kChunkLog2 + 5);
 
 int main() {
   char op[16];
@@ -14,6 +16,15 @@ int main() {
   while (std::scanf("%15s %llu %llu", op, &a, &b) == 3) {
     if (std::strcmp(op, "jump") == 0) {
       std::printf("%llu\n", static_cast<unsigned long long>(fsa::jump_host(kTables, a, b)));
+    } else if (std::strcmp(op, "chunk") == 0) {
+      // start state of chunk b of a row with initial state a
+      std::printf("%llu\n", static_cast<unsigned long long>(
+                                 fsa::chunk_start_host(kTables, kLanes1, kLanes2, a, b)));
+    } else if (std::strcmp(op, "stepmul") == 0) {
+      // b steps with the multiply form of the xorshift step
+      uint32_t lo = static_cast<uint32_t>(a), hi = static_cast<uint32_t>(a >> 32);
+      for (unsigned long long k = 0; k < b; ++k) fsa::xorshift_step_mul(lo, hi, fsa::kShiftMultipliers);
+      std::printf("%llu\n", (static_cast<unsigned long long>(hi) << 32) | lo);
     } else if (std::strcmp(op, "draw") == 0) {
       std::printf("%u\n", fsa::bounded_draw(a, static_cast<uint32_t>(b)));
     } else if (std::strcmp(op, "seed") == 0) {

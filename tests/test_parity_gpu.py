@@ -144,6 +144,20 @@ def test_2hop_ids_and_outputs_bit_exact(name, fan, seed):
     assert_bit_equal(out, ref_out)
 
 
+@pytest.mark.parametrize("name", ["powerlaw", "hub", "uniform"])
+@pytest.mark.parametrize("seed", [3, U64_MAX])
+def test_hub_roots_bit_exact(name, seed):
+    """Roots = the highest-degree nodes: every first-hop row is long and the
+    first-hop draws of a root are spread over the whole CTA."""
+    out, s1, s2, ref_out, r1, r2 = run_2hop(name, 15, 10, seed, root_seed=-1, batch=96)
+    np.testing.assert_array_equal(s1.cpu().numpy(), r1)
+    np.testing.assert_array_equal(s2.cpu().numpy(), r2)
+    assert_bit_equal(out, ref_out)
+    out, s, t, ref_out, rs, rt = run_1hop(name, 10, seed, root_seed=-1, batch=96)
+    np.testing.assert_array_equal(s.cpu().numpy(), rs)
+    assert_bit_equal(out, ref_out)
+
+
 @pytest.mark.parametrize("dim", [1, 2, 3, 4, 8, 16, 33, 64, 100, 127, 128, 129, 256, 602, 1000])
 def test_2hop_feature_widths(dim):
     out, _, _, ref_out, _, _ = run_2hop("powerlaw", 15, 10, 7, dim=dim, batch=64)
@@ -253,6 +267,10 @@ def test_launch_count_advances():
     x = cpu_features(8, 12).cuda()
     before = fsa.launch_count()
     fsa.fused_sample_agg_2hop(rp, cl, x, frontier("toy").cuda(), 3, 2)
+    # plan, scan, draws, gather
+    assert fsa.launch_count() == before + 4
+    before = fsa.launch_count()
+    fsa.fused_sample_agg(rp, cl, x, frontier("toy").cuda(), 3)
     assert fsa.launch_count() == before + 1
 
 

@@ -76,3 +76,23 @@ def test_row_seeds_match_oracle(run):
         got = run([f"seed {base} {root}"])[0].split()
         assert int(got[0]) == oracle.row_state(base, root, 1, 3)
         assert int(got[1]) == oracle.row_state(base, root, 0, root)
+
+
+def test_chunk_start_equals_serial_steps(run):
+    rng = random.Random(5)
+    chunk = 32
+    js = [0, 1, 2, 5, 31, 32, 33, 63, 64, 65, 100, 127, 128, 500, 1023, 1024, 1025, 4097,
+          33_000, 16_000_000 // chunk]
+    cases = [(rng.getrandbits(64) | 1, j) for j in js]
+    got = run([f"chunk {s} {j}" for s, j in cases])
+    want = [str(oracle.xorshift_advance(s, j * chunk)) for s, j in cases]
+    assert got == want
+
+
+def test_multiply_form_of_xorshift_step(run):
+    rng = random.Random(6)
+    cases = [(rng.getrandbits(64), n) for n in (1, 2, 3, 10, 1000)]
+    cases += [(U64, 5), (1, 7), (1 << 63, 3), (0x9E3779B97F4A7C15, 64)]
+    got = run([f"stepmul {s} {n}" for s, n in cases])
+    want = [str(oracle.xorshift_advance(s, n)) for s, n in cases]
+    assert got == want

@@ -77,3 +77,14 @@ def test_workload_table():
     assert (w.num_nodes, w.dim, w.fanouts, w.batch) == (2_450_000, 100, (15, 10), 1024)
     assert synthetic.WORKLOADS["c1_1hop_uniform"].fanouts == (10,)
     assert synthetic.WORKLOADS["c5_2hop_100m"].batch == 65_536
+
+
+def test_root_batches_are_not_degree_biased():
+    """Root batches and graphs use separate random streams: the mean degree
+    of a uniform root batch matches the graph's mean degree (a shared stream
+    once made root batch 0 the graph's 1024 largest hubs)."""
+    g = synthetic.chung_lu_graph(50_000, 1_000_000, 2.1, 5_000, seed=0)
+    deg = g.degrees().to(torch.float64)
+    for seed in (0, 1, 2):
+        r = synthetic.root_batch(g.num_nodes, 2_000, seed=seed).long()
+        assert float(deg[r].mean()) < 2.0 * float(deg.mean())
