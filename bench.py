@@ -338,7 +338,7 @@ def kernel_times(w, inp: Inputs, iters: int) -> dict:
     s1 = torch.empty((B, k1), dtype=torch.int32, device=dev)
     s2 = torch.empty((B, k1, k2), dtype=torch.int32, device=dev)
     grad = torch.empty((n, D), device=dev)
-    ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, k1, k2, D, 1, 1)
+    ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, k1, k2, 1, 1)
     ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
     names = ("fill", "fwd", "bwd")
@@ -353,7 +353,7 @@ def kernel_times(w, inp: Inputs, iters: int) -> dict:
         _lib.check(L.fsa_sample_agg_2hop_forward(
             inp.rowptr.data_ptr(), inp.col.data_ptr(), n, inp.col.numel(), x.data_ptr(), D,
             inp.frontiers[j].data_ptr(), B, inp.offset, k1, k2, inp.seeds[j], out.data_ptr(),
-            s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, stream), "fwd")
+            s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, None, 0, stream), "fwd")
         ev[2].record()
         _lib.check(L.fsa_sample_agg_2hop_backward(
             inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,

@@ -20,8 +20,6 @@ draws exactly the samples the whole batch would.
 
 from __future__ import annotations
 
-import functools
-
 import torch
 
 from . import _lib
@@ -139,65 +137,17 @@ def _ptr(t):
     return t.data_ptr() if t is not None else None
 
 
-_SIDE_STREAMS: dict[int, torch.cuda.Stream] = {}
-_PRIORITY_STREAMS: dict[int, torch.cuda.Stream] = {}
-
-
-def _side_stream(device: torch.device) -> torch.cuda.Stream:
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    s = _SIDE_STREAMS.get(idx)
-    if s is None:
-        s = torch.cuda.Stream(device=idx)
-        _SIDE_STREAMS[idx] = s
-    return s
-
-
-def _priority_stream(device: torch.device) -> torch.cuda.Stream:
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    s = _PRIORITY_STREAMS.get(idx)
-    if s is None:
-        s = torch.cuda.Stream(device=idx, priority=-1)
-        _PRIORITY_STREAMS[idx] = s
-    return s
-
-
 def _zeroed(num_nodes: int, dim: int, device: torch.device, stream: int) -> torch.Tensor:
     grad = torch.empty((num_nodes, dim), dtype=torch.float32, device=device)
     _lib.check(_L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fsa_fill_zero_f32")
     return grad
 
 
-class _PendingGrad:
-    """A dense gradient buffer whose zero-fill was launched on a side stream
-    during the forward, so that the memory-bound fill overlaps the
-    compute-bound sampling kernels; the backward waits for it and scatters
-    into it (the reference allocates it with at::zeros inside the backward,
-    fuseop/binding.cpp:137, :220)."""
-
-    __slots__ = ("grad", "done")
-
-    def __init__(self, num_nodes: int, dim: int, device: torch.device):
-        cur = torch.cuda.current_stream(device)
-        side = _side_stream(device)
-        self.grad = torch.empty((num_nodes, dim), dtype=torch.float32, device=device)
-        side.wait_stream(cur)  # the block may have been in use on `cur`
-        _lib.check(_L.fsa_fill_zero_f32(self.grad.data_ptr(), self.grad.numel(),
-                                        side.cuda_stream), "fsa_fill_zero_f32")
-        self.grad.record_stream(side)
-        self.done = torch.cuda.Event()
-        self.done.record(side)
-
-    def take(self) -> torch.Tensor:
-        torch.cuda.current_stream(self.grad.device).wait_event(self.done)
-        g, self.grad = self.grad, None
-        return g
-
-
 def _grad_buffer(zeroed, num_nodes, dim, device, stream) -> torch.Tensor:
-    if zeroed is not None:
-        g = zeroed.take()
-        if tuple(g.shape) == (num_nodes, dim) and g.device == device:
-            return g
+    """The dense gradient: the buffer the forward already zeroed, else a new
+    zero-filled one (the reference's at::zeros, fuseop/binding.cpp:137, :220)."""
+    if zeroed is not None and tuple(zeroed.shape) == (num_nodes, dim) and zeroed.device == device:
+        return zeroed
     return _zeroed(num_nodes, dim, device, stream)
 
 
@@ -229,7 +179,7 @@ def _forward_1hop(rowptr, col, x, frontier, fanout, seed, capture, batch_offset=
     return out, samples, takes
 
 
-def _backward_1hop(samples, takes, grad_out, num_nodes, zeroed=None):
+def _backward_1hop(samples, takes, grad_out, num_nodes):
     if not (samples.is_cuda and takes.is_cuda and grad_out.is_cuda):
         raise RuntimeError("backward inputs must be CUDA tensors")
     if samples.dtype != torch.int32 or takes.dtype != torch.int32:
@@ -249,7 +199,7 @@ def _backward_1hop(samples, takes, grad_out, num_nodes, zeroed=None):
     B, D = grad_out.shape
     with _DeviceGuard(grad_out.device):
         stream = _stream_handle(grad_out.device)
-        grad_x = _grad_buffer(zeroed, num_nodes, D, grad_out.device, stream)
+        grad_x = _zeroed(num_nodes, D, grad_out.device, stream)
         if B == 0 or samples.size(1) == 0:
             return grad_x
         status = _L.fsa_sample_agg_backward(
@@ -260,7 +210,7 @@ def _backward_1hop(samples, takes, grad_out, num_nodes, zeroed=None):
 
 
 def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, batch_offset=0,
-                  overlap=False):
+                  zero=None):
     _check_graph_inputs(rowptr, col, x, frontier)
     fanout1 = _as_int64(fanout1, "fanout1")
     fanout2 = _as_int64(fanout2, "fanout2")
@@ -274,31 +224,21 @@ def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, bat
             out = torch.zeros((B, D), dtype=x.dtype, device=dev)
             s1 = torch.full((B, fanout1), -1, dtype=torch.int32, device=dev)
             s2 = torch.full((B, fanout1, fanout2), -1, dtype=torch.int32, device=dev)
+            if zero is not None:
+                zero.zero_()
             return out, s1, s2
         out = torch.empty((B, D), dtype=x.dtype, device=dev)
         s1 = torch.empty((B, fanout1), dtype=torch.int32, device=dev) if capture else None
         s2 = torch.empty((B, fanout1, fanout2), dtype=torch.int32, device=dev) if capture else None
-        ws_bytes = _L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, D, int(capture),
+        ws_bytes = _L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, int(capture),
                                                          int(capture))
         ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
-        launch = functools.partial(
-            _L.fsa_sample_agg_2hop_forward,
+        zero_ptr = zero.data_ptr() if zero is not None else None
+        zero_count = zero.numel() if zero is not None else 0
+        status = _L.fsa_sample_agg_2hop_forward(
             rowptr.data_ptr(), col.data_ptr(), x.size(0), col.numel(), x.data_ptr(), D,
             frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(), _ptr(s1),
-            _ptr(s2), ws.data_ptr(), ws_bytes)
-        if overlap:
-            # While the gradient zero-fill runs on a side stream, launch the
-            # sampling kernels on a high-priority stream so that the block
-            # scheduler prefers them over the fill's CTAs.  Outputs and
-            # workspace were allocated on the caller's stream, which waits for
-            # this work before anything after the call.
-            cur = torch.cuda.current_stream(dev)
-            hi = _priority_stream(dev)
-            hi.wait_stream(cur)
-            status = launch(hi.cuda_stream)
-            cur.wait_stream(hi)
-        else:
-            status = launch(_stream_handle(dev))
+            _ptr(s2), ws.data_ptr(), ws_bytes, zero_ptr, zero_count, _stream_handle(dev))
         _lib.check(status, "fsa_sample_agg_2hop_forward")
     return out, s1, s2
 
@@ -346,12 +286,9 @@ class _FusedSampleAggFn(torch.autograd.Function):
         out, samples, takes = _forward_1hop(
             rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
             fanout, replay_seed, capture, batch_offset)
-        ctx.pending = None
         if capture:
             ctx.save_for_backward(samples, takes)
             ctx.num_nodes = int(x.size(0))
-            if ctx.needs_input_grad[2]:
-                ctx.pending = _PendingGrad(ctx.num_nodes, x.size(1), x.device)
         ctx.capture = capture
         return out
 
@@ -360,9 +297,7 @@ class _FusedSampleAggFn(torch.autograd.Function):
         grad_x = None
         if ctx.capture and ctx.needs_input_grad[2]:
             samples, takes = ctx.saved_tensors
-            grad_x = _backward_1hop(samples, takes, grad_out.contiguous(), ctx.num_nodes,
-                                    ctx.pending)
-        ctx.pending = None
+            grad_x = _backward_1hop(samples, takes, grad_out.contiguous(), ctx.num_nodes)
         return None, None, grad_x, None, None, None, None, None
 
 
@@ -372,13 +307,18 @@ class _FusedSampleAgg2HopFn(torch.autograd.Function):
                 batch_offset):
         _check_python_inputs(rowptr, col, x, frontier)
         capture = bool(save_indices) or x.requires_grad
-        ctx.pending = None
-        prefill = capture and ctx.needs_input_grad[2]
-        if prefill:
-            ctx.pending = _PendingGrad(int(x.size(0)), x.size(1), x.device)
+        # When the backward will need the dense feature gradient, allocate it
+        # now and let the forward's sampling kernel zero it: that kernel is
+        # bound by integer issue, the fill by HBM writes, so the fill costs
+        # little extra (the reference zero-fills inside the backward,
+        # fuseop/binding.cpp:220).
+        ctx.grad_buffer = None
+        if capture and ctx.needs_input_grad[2]:
+            ctx.grad_buffer = torch.empty((x.size(0), x.size(1)), dtype=torch.float32,
+                                          device=x.device)
         out, s1, s2 = _forward_2hop(
             rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
-            fanout1, fanout2, replay_seed, capture, batch_offset, overlap=prefill)
+            fanout1, fanout2, replay_seed, capture, batch_offset, zero=ctx.grad_buffer)
         if capture:
             ctx.save_for_backward(s1, s2)
             ctx.num_nodes = int(x.size(0))
@@ -390,8 +330,9 @@ class _FusedSampleAgg2HopFn(torch.autograd.Function):
         grad_x = None
         if ctx.capture and ctx.needs_input_grad[2]:
             s1, s2 = ctx.saved_tensors
-            grad_x = _backward_2hop(grad_out.contiguous(), s1, s2, ctx.num_nodes, ctx.pending)
-        ctx.pending = None
+            grad_x = _backward_2hop(grad_out.contiguous(), s1, s2, ctx.num_nodes,
+                                    ctx.grad_buffer)
+        ctx.grad_buffer = None
         return None, None, grad_x, None, None, None, None, None, None
 
 

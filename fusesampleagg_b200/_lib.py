@@ -34,10 +34,10 @@ SIGNATURES = {
         _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _u64, _p, _p, _p, _p]),
     "fsa_sample_agg_backward": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _p, _i64, _p]),
-    "fsa_sample_agg_2hop_workspace_size": (ctypes.c_size_t, [_i64, _i32, _i32, _i64, _int, _int]),
+    "fsa_sample_agg_2hop_workspace_size": (ctypes.c_size_t, [_i64, _i32, _i32, _int, _int]),
     "fsa_sample_agg_2hop_forward": (
         _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p,
-               _p, ctypes.c_size_t, _p]),
+               _p, ctypes.c_size_t, _p, _i64, _p]),
     "fsa_sample_agg_2hop_backward": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),

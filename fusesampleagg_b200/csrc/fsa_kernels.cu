@@ -366,6 +366,10 @@ constexpr int kThreadsScan = 1024;
 constexpr int kThreadsDraw = 256;
 constexpr int kThreadsGather = 256;
 
+// Draws of a second-hop row are processed in groups of 32 chunks (one chunk
+// per lane, kGroupDraws draws); a warp takes one group at a time.
+constexpr uint32_t kGroupDraws = 32u * kChunk;
+
 struct Plan2Args {
   const int32_t* rowptr;
   const int32_t* col;
@@ -382,19 +386,19 @@ struct Plan2Args {
   int32_t* mbeg;             // [R = B*k1] begin of each second-hop row
   int32_t* mtake;            // [R] reservoir size of each second-hop row
   int32_t* mdraws;           // [R] draws of each second-hop row
-  int32_t* nchunks;          // [R] kChunk-draw chunks of each second-hop row
   unsigned long long* state; // [R] initial xorshift state of each second-hop row
-  unsigned int* done;        // [B] gather-kernel slot counters, reset here
-  unsigned long long* next;  // draw-kernel work counter, reset here
+  long long* lpre;           // [R] group prefix of the row within its root
+  long long* rgroups;        // [B] groups of all second-hop rows of a root
+  unsigned long long* next;  // draw-kernel fill-block counter, reset here
 };
 
 __global__ void __launch_bounds__(kThreadsPlan)
     fsa_2hop_plan_kernel(const Plan2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* s1 = reinterpret_cast<int*>(smem_raw);  // [k1] winners, then ids
+  long long* groups = reinterpret_cast<long long*>(smem_raw + ((4 * a.fanout1 + 15) & ~15));
   const int k1 = a.fanout1;
   const int k2 = a.fanout2;
-  const int64_t k12 = static_cast<int64_t>(k1) * k2;
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
   const int64_t N = a.num_nodes;
@@ -412,8 +416,6 @@ __global__ void __launch_bounds__(kThreadsPlan)
     }
     const int take1 = rdegree < k1 ? rdegree : k1;
     for (int i = tid; i < k1; i += nthreads) s1[i] = -1;
-    for (int64_t e = tid; e < k12; e += nthreads) a.win2[b * k12 + e] = -1;
-    if (tid == 0) a.done[b] = 0;
     __syncthreads();
     if (rdegree > take1) {
       const uint64_t s0 = fsa::row_state(a.seed, static_cast<uint64_t>(root), 0,
@@ -441,22 +443,35 @@ __global__ void __launch_bounds__(kThreadsPlan)
       a.mbeg[r] = mb;
       a.mtake[r] = mt;
       a.mdraws[r] = md - mt;
-      a.nchunks[r] = static_cast<int32_t>((static_cast<uint32_t>(md - mt) + kChunk - 1) / kChunk);
       a.state[r] = fsa::row_state(a.seed, static_cast<uint64_t>(root), 1, static_cast<uint64_t>(i));
+      groups[i] = (static_cast<long long>(md - mt) + kGroupDraws - 1) / kGroupDraws;
+    }
+    // Every second-hop slot starts as "kept" (no winner).
+    for (int64_t e = tid; e < static_cast<int64_t>(k1) * k2; e += nthreads) {
+      a.win2[b * k1 * k2 + e] = -1;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      long long run = 0;
+      for (int i = 0; i < k1; ++i) {
+        a.lpre[b * k1 + i] = run;
+        run += groups[i];
+      }
+      a.rgroups[b] = run;
     }
     __syncthreads();
   }
 }
 
 struct Scan2Args {
-  const int32_t* nchunks;  // [R]
-  long long* pre;          // [R + 1] exclusive prefix, pre[R] = total chunks
-  int64_t rows;
+  const long long* counts;  // [n]
+  long long* pre;           // [n + 1] exclusive prefix, pre[n] = total
+  int64_t n;
 };
 
 constexpr int kScanItems = 4;
 
-// One CTA, tiles of blockDim * kScanItems rows: each thread scans its
+// One CTA, tiles of blockDim * kScanItems entries: each thread scans its
 // contiguous items, warp shuffles and the warp totals give the tile prefix,
 // a running carry joins the tiles.
 __global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2Args a) {
@@ -469,13 +484,13 @@ __global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2
   if (tid == 0) carry = 0;
   __syncthreads();
   const int64_t tile = static_cast<int64_t>(blockDim.x) * kScanItems;
-  for (int64_t t0 = 0; t0 < a.rows; t0 += tile) {
+  for (int64_t t0 = 0; t0 < a.n; t0 += tile) {
     const int64_t i0 = t0 + static_cast<int64_t>(tid) * kScanItems;
     long long v[kScanItems];
     long long local = 0;
 #pragma unroll
     for (int u = 0; u < kScanItems; ++u) {
-      v[u] = i0 + u < a.rows ? a.nchunks[i0 + u] : 0;
+      v[u] = i0 + u < a.n ? a.counts[i0 + u] : 0;
       local += v[u];
     }
     long long incl = local;
@@ -499,75 +514,165 @@ __global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2
     long long run = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - local;
 #pragma unroll
     for (int u = 0; u < kScanItems; ++u) {
-      if (i0 + u < a.rows) a.pre[i0 + u] = run;
+      if (i0 + u < a.n) a.pre[i0 + u] = run;
       run += v[u];
     }
     __syncthreads();
     if (tid == 0) carry += warp_sums[nw - 1];
     __syncthreads();
   }
-  if (tid == 0) a.pre[a.rows] = carry;
+  if (tid == 0) a.pre[a.n] = carry;
 }
 
 struct Draw2Args {
-  const long long* pre;              // [R + 1] chunk prefix over second-hop rows
+  const long long* rpre;             // [B + 1] group prefix over roots
+  const long long* lpre;             // [R] group prefix of each row within its root
   const unsigned long long* state;   // [R]
   const int32_t* mtake;              // [R]
   const int32_t* mdraws;             // [R]
-  int64_t rows;                      // R = B * k1
+  int64_t batch_size;
+  int fanout1;
   int fanout2;
-  int32_t* win2;                     // [R][k2]
-  unsigned long long* next;          // work counter (chunks handed out so far)
+  int32_t* win2;                     // [R][k2] winners
+  unsigned long long* next;          // fill-block counter
+  float4* fill;                      // optional buffer to zero (16-byte aligned)
+  int64_t fill_vec4;                 // float4 elements of `fill`
+  int smem_roots;                    // rpre staged in shared memory when B < this
 };
 
-// Largest r in [lo, hi] with pre[r] <= q (pre[lo] <= q holds).
-__device__ __forceinline__ int64_t row_of(const long long* pre, int64_t lo, int64_t hi,
-                                          long long q) {
-  while (lo < hi) {
-    const int64_t mid = (lo + hi + 1) >> 1;
-    if (__ldg(pre + mid) <= q) lo = mid; else hi = mid - 1;
+// Fill work item: kFillItemVec4 float4 stores per lane (32 KB per warp); a
+// warp takes up to kFillPerGroup of them after each draw group.
+constexpr int kFillItemVec4 = 64;
+constexpr int kFillPerGroup = 2;
+constexpr int kSmemRoots = 4096;
+
+// Largest idx in [0, n) with arr[idx] <= key, given arr[0] <= key and arr
+// non-decreasing: a 32-way search, one probe per lane per round.  Must be
+// called by all 32 lanes with the same arguments.
+__device__ __forceinline__ int64_t warp_search(const long long* arr, int64_t n, long long key,
+                                               int lane) {
+  int64_t lo = 0, hi = n - 1;
+  while (hi > lo) {
+    const int64_t step = (hi - lo + 32) / 32;
+    const int64_t idx = lo + lane * step;
+    const bool ok = idx <= hi && arr[idx] <= key;
+    const unsigned m = __ballot_sync(0xffffffffU, ok);
+    const int k = 31 - __clz(m);
+    lo += k * step;
+    hi = min(hi, lo + step - 1);
   }
   return lo;
 }
 
-// Persistent grid; each warp repeatedly takes the next 32 chunks of the
-// global chunk sequence (second-hop rows in (root, slot) order, each row's
-// chunks in position order), one chunk per lane.  Lane 0 binary-searches the
-// row of the first chunk; the other lanes find theirs among the next 32 row
-// boundaries with a shuffle search.
+// Zeroes fill block `idx` (32 KB) with streaming stores.
+__device__ __forceinline__ void fill_block(float4* fill, int64_t fill_vec4, long long idx,
+                                           int lane) {
+  const long long v0 = idx * 32LL * kFillItemVec4 + lane;
+  const float4 z = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+#pragma unroll 8
+  for (int k = 0; k < kFillItemVec4; ++k) {
+    const long long v = v0 + 32LL * k;
+    if (v < fill_vec4) __stcs(fill + v, z);
+  }
+}
+
+// Persistent grid.  Warp w draws groups w, w + W, w + 2W, ... of the global
+// group sequence (roots in batch order, their second-hop rows in slot order,
+// each row's groups in position order); the per-group set-up is a few
+// dependent loads: the root is found in a shared-memory copy of the root
+// prefix, the root's row descriptors are read lane-parallel in one round,
+// the group's part of the jump is one broadcast table product and the
+// lane's part one more.  Lane l of group g of a row runs chunk 32 g + l.
+//
+// Optionally the warps also zero a buffer (the backward's dense gradient)
+// in 32 KB blocks taken from a shared counter between draw groups: the draw
+// loop is bound by integer issue, the fill by HBM writes.
 __global__ void __launch_bounds__(kThreadsDraw) fsa_2hop_draw_kernel(const Draw2Args a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  long long* s_rpre = reinterpret_cast<long long*>(smem_raw);  // [B + 1] when staged
   const int lane = threadIdx.x & 31;
-  const int64_t R = a.rows;
-  const long long total = __ldg(a.pre + R);
-  while (true) {
-    unsigned long long base = 0;
-    if (lane == 0) base = atomicAdd(a.next, 32ULL);
-    base = __shfl_sync(0xffffffffU, base, 0);
-    if (static_cast<long long>(base) >= total) break;
-    const long long q0 = static_cast<long long>(base);
-    const long long q = q0 + lane;
-    int64_t r0 = 0;
-    if (lane == 0) r0 = row_of(a.pre, 0, R - 1, q0);
-    r0 = __shfl_sync(0xffffffffU, r0, 0);
-    // e = pre[r0 + 1 + lane]; this lane's row is r0 + #{m : e_m <= q}.
-    const int64_t ei = r0 + 1 + lane;
-    const long long e = ei <= R ? __ldg(a.pre + ei) : LLONG_MAX;
-    int c = 0;
-#pragma unroll
-    for (int step = 16; step > 0; step >>= 1) {
-      const long long em = __shfl_sync(0xffffffffU, e, c + step - 1);
-      if (em <= q) c += step;
+  const int64_t B = a.batch_size;
+  const int k1 = a.fanout1;
+  const int k2 = a.fanout2;
+  const bool staged = B < a.smem_roots;
+  if (staged) {
+    for (int64_t t = threadIdx.x; t <= B; t += blockDim.x) s_rpre[t] = __ldg(a.rpre + t);
+  }
+  __syncthreads();
+  const long long total = staged ? s_rpre[B] : __ldg(a.rpre + B);
+  const long long nfill = (a.fill_vec4 + 32LL * kFillItemVec4 - 1) / (32LL * kFillItemVec4);
+  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  bool fill_left = nfill > 0;
+
+  for (long long G = warp_id; G < total; G += nwarps) {
+    const int64_t b = staged ? warp_search(s_rpre, B, G, lane) : warp_search(a.rpre, B, G, lane);
+    const long long local = G - (staged ? s_rpre[b] : __ldg(a.rpre + b));
+    // Slot within the root, and that row's fields.
+    int i;
+    uint32_t take, nd;
+    uint64_t s0;
+    long long lpi;
+    if (k1 <= 32) {
+      // One round: lane l reads row l of the root; the slot is the last row
+      // whose group prefix is <= local.
+      const int64_t rl = b * k1 + lane;
+      const bool in = lane < k1;
+      const long long lp = in ? __ldg(a.lpre + rl) : LLONG_MAX;
+      const int tk = in ? __ldg(a.mtake + rl) : 0;
+      const int dr = in ? __ldg(a.mdraws + rl) : 0;
+      const unsigned long long st = in ? __ldg(a.state + rl) : 0ULL;
+      const unsigned m = __ballot_sync(0xffffffffU, lp <= local);
+      i = 31 - __clz(m);
+      take = static_cast<uint32_t>(__shfl_sync(0xffffffffU, tk, i));
+      nd = static_cast<uint32_t>(__shfl_sync(0xffffffffU, dr, i));
+      s0 = __shfl_sync(0xffffffffU, st, i);
+      lpi = __shfl_sync(0xffffffffU, lp, i);
+    } else {
+      i = static_cast<int>(warp_search(a.lpre + b * k1, k1, local, lane));
+      const int64_t ri = b * k1 + i;
+      take = static_cast<uint32_t>(__ldg(a.mtake + ri));
+      nd = static_cast<uint32_t>(__ldg(a.mdraws + ri));
+      s0 = __ldg(a.state + ri);
+      lpi = __ldg(a.lpre + ri);
     }
-    // Every lane takes part in the shuffle (a full-mask shuffle reached by
-    // only some lanes never completes).
-    const long long e_last = __shfl_sync(0xffffffffU, e, 31);
-    if (c == 31 && e_last <= q) c = 32;
-    if (q >= total) continue;
-    int64_t r = r0 + c;
-    if (c == 32) r = row_of(a.pre, r0 + 32, R - 1, q);  // > 32 row boundaries in 32 chunks
-    const uint32_t j = static_cast<uint32_t>(q - __ldg(a.pre + r));
-    row_chunk(__ldg(a.state + r), static_cast<uint32_t>(__ldg(a.mtake + r)),
-              static_cast<uint32_t>(__ldg(a.mdraws + r)), j, a.win2 + r * a.fanout2);
+    const int64_t r = b * k1 + i;
+    const uint32_t g = static_cast<uint32_t>(local - lpi);
+    // Group part of the jump (warp-uniform): T^(g * kGroupDraws) s0.
+    uint64_t sg = s0;
+    if (g & 31) sg = apply_table(&g_lanes2.v[g & 31][0][0], sg);
+    uint32_t hi = g >> 5;
+#pragma unroll 1
+    while (hi != 0) {
+      const int bit = __ffs(hi) - 1;
+      hi &= hi - 1;
+      sg = apply_table(&g_jump.v[fsa::kChunkLog2 + 10 + bit][0][0], sg);
+    }
+    const uint32_t off = (g * 32u + static_cast<uint32_t>(lane)) * kChunk;
+    if (off < nd) {
+      const uint64_t st = lane != 0 ? apply_table(&g_lanes1.v[lane][0][0], sg) : sg;
+      chunk_draws(st, take + off, nd - off < kChunk ? nd - off : kChunk, take,
+                  a.win2 + r * k2);
+    }
+    // A few fill blocks between draw groups.
+    for (int f = 0; f < kFillPerGroup && fill_left; ++f) {
+      unsigned long long item = 0;
+      if (lane == 0) item = atomicAdd(a.next, 1ULL);
+      item = __shfl_sync(0xffffffffU, item, 0);
+      if (static_cast<long long>(item) >= nfill) {
+        fill_left = false;
+      } else {
+        fill_block(a.fill, a.fill_vec4, static_cast<long long>(item), lane);
+      }
+    }
+  }
+  // Whatever fill is left once the draws are done.
+  while (fill_left) {
+    unsigned long long item = 0;
+    if (lane == 0) item = atomicAdd(a.next, 1ULL);
+    item = __shfl_sync(0xffffffffU, item, 0);
+    if (static_cast<long long>(item) >= nfill) break;
+    fill_block(a.fill, a.fill_vec4, static_cast<long long>(item), lane);
   }
 }
 
@@ -579,130 +684,134 @@ struct Gather2Args {
   int64_t batch_size;
   int fanout1;
   int fanout2;
-  const int32_t* mbeg;
-  const int32_t* mtake;
-  int32_t* win2;       // [B][k1][k2] winners in, second-hop ids out (in place)
-  float* inner;        // [B][k1][D] slot means (workspace)
-  int32_t* mvalid;     // [B][k1] valid leaves per slot (workspace)
-  unsigned int* done;  // [B] slots finished per root, zeroed by the plan kernel
+  const int32_t* mbeg;   // [B*k1]
+  const int32_t* mtake;  // [B*k1]
+  const int32_t* win2;   // [B][k1][k2] winners (position of the last hit, -1 = kept)
+  int32_t* samples2;     // optional id output; may alias win2
   float* out;
+  int dchunk;            // feature tile width (multiple of the vector width)
 };
 
-// Rows gathered per batch of independent loads (per lane).
-constexpr int kGatherBatch = 8;
+// Shared-memory layout of the gather kernel, in bytes.
+struct LayoutG {
+  int inner, s2, mvalid, total;
+};
 
-// Inner sum of one (slot, feature vector): valid leaves in j order from 0.0f.
-template <int V>
-__device__ __forceinline__ VecF<V> leaf_sum(const int32_t* leaves, int k2, const float* base,
-                                            int64_t D, int64_t N) {
-  VecF<V> acc;
-  vzero(acc);
-  for (int j0 = 0; j0 < k2; j0 += kGatherBatch) {
-    VecF<V> r[kGatherBatch];
-    bool ok[kGatherBatch];
-#pragma unroll
-    for (int u = 0; u < kGatherBatch; ++u) {
-      const int32_t leaf = j0 + u < k2 ? leaves[j0 + u] : -1;
-      ok[u] = leaf >= 0 && leaf < N;
-      if (ok[u]) r[u] = load_stream<V>(base + static_cast<int64_t>(leaf) * D);
-    }
-#pragma unroll
-    for (int u = 0; u < kGatherBatch; ++u) {
-      if (ok[u]) {
-#pragma unroll
-        for (int c = 0; c < V; ++c) acc.v[c] += r[u].v[c];
-      }
-    }
-  }
-  return acc;
+__host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
+
+__host__ __device__ inline LayoutG layout_gather(int k1, int k2, int dchunk) {
+  LayoutG l;
+  l.inner = 0;                              // float [k1][dchunk]
+  l.s2 = align16(4 * k1 * dchunk);          // int32 [k1 * k2]
+  l.mvalid = align16(l.s2 + 4 * k1 * k2);   // int32 [k1]
+  l.total = align16(l.mvalid + 4 * k1);
+  return l;
 }
 
-// One warp per (root, first-hop slot), no CTA barriers.  The warp resolves
-// the slot's winners to leaf ids (written back in place: they are the
-// saved samples2 when requested), gathers the leaf rows and writes the slot
-// mean (inner sum over j in order / valid) to a scratch row.  The last warp
-// to finish a root -- device-scope fence, then a counter; nothing waits --
-// sums the slot means in slot order and divides by the non-empty count
-// (fused_sample_agg.cu:189-213), so outputs keep the reference's bits.
+// Rows gathered per batch of independent loads (per thread).
+constexpr int kGatherBatch = 8;
+
+// CTA per root.  Items are (first-hop slot, feature vector) pairs: an item
+// sums its slot's valid leaf rows in j order from 0.0f (loads batched so
+// that kGatherBatch rows are in flight per thread) and divides by the valid
+// count; then the slot means are summed in slot order and divided by the
+// non-empty count (fused_sample_agg.cu:189-213).
 template <int V>
-__global__ void __launch_bounds__(kThreadsGather, 4)
+__global__ void __launch_bounds__(kThreadsGather)
     fsa_2hop_gather_kernel(const Gather2Args a) {
-  const int lane = threadIdx.x & 31;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   const int k1 = a.fanout1;
   const int k2 = a.fanout2;
-  const int64_t k12 = static_cast<int64_t>(k1) * k2;
+  const LayoutG L = layout_gather(k1, k2, a.dchunk);
+  float* inner = reinterpret_cast<float*>(smem_raw + L.inner);
+  int* s2 = reinterpret_cast<int*>(smem_raw + L.s2);
+  int* mvalid = reinterpret_cast<int*>(smem_raw + L.mvalid);
+  const int tid = threadIdx.x;
+  const int nthreads = blockDim.x;
+  const int k12 = k1 * k2;
   const int64_t D = a.feature_dim;
   const int64_t N = a.num_nodes;
-  const int64_t nv = D / V;
-  const int64_t nslots = a.batch_size * k1;
-  const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       w < nslots; w += wstride) {
-    const int64_t b = w / k1;
-    const int i = static_cast<int>(w - b * k1);
-    // ---- winners -> leaf ids (the serial loop's final reservoir) ----------
-    const int t = __ldg(a.mtake + w);
-    const int mb = __ldg(a.mbeg + w);
-    int32_t* leaves = a.win2 + b * k12 + static_cast<int64_t>(i) * k2;
-    int valid = 0;
-    for (int j = lane; j < k2; j += 32) {
+
+  for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
+    // Winners -> second-hop ids: slot j of a row holds col[winner], or
+    // col[j] if no draw replaced it -- the serial loop's final reservoir.
+    for (int e = tid; e < k12; e += nthreads) {
+      const int i = e / k2;
+      const int j = e - i * k2;
+      const int64_t r = b * k1 + i;
       int32_t id = -1;
-      if (j < t) {
-        const int win = leaves[j];
-        id = __ldg(a.col + static_cast<int64_t>(mb) + (win >= 0 ? win : j));
+      if (j < __ldg(a.mtake + r)) {
+        const int w = a.win2[b * k12 + e];
+        id = __ldg(a.col + static_cast<int64_t>(__ldg(a.mbeg + r)) + (w >= 0 ? w : j));
       }
-      leaves[j] = id;
-      if (id >= 0) {
-        if (id < N) ++valid; else flag_status(FSA_STATUS_BAD_NEIGHBOR);
-      }
+      s2[e] = id;
+      if (a.samples2 != nullptr) a.samples2[b * k12 + e] = id;
     }
+    __syncthreads();
+    for (int64_t f0 = 0; f0 < D; f0 += a.dchunk) {
+      const int fc = static_cast<int>(D - f0 < a.dchunk ? D - f0 : a.dchunk);
+      const int nv = fc / V;
+      const int items = k1 * nv;
+      for (int it = tid; it < items; it += nthreads) {
+        const int i = it / nv;
+        const int v = it - i * nv;
+        const int32_t* leaves = s2 + i * k2;
+        const float* base = a.x + f0 + v * V;
+        VecF<V> acc;
+        vzero(acc);
+        int valid = 0;
+        for (int j0 = 0; j0 < k2; j0 += kGatherBatch) {
+          VecF<V> rows[kGatherBatch];
+          bool ok[kGatherBatch];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) valid += __shfl_xor_sync(0xffffffffU, valid, o);
-    __syncwarp();
-    // ---- slot mean --------------------------------------------------------
-    float* slot_mean = a.inner + w * D;
-    if (valid > 0) {
-      const float denom = static_cast<float>(valid);
-      for (int64_t v = lane; v < nv; v += 32) {
-        VecF<V> acc = leaf_sum<V>(leaves, k2, a.x + v * V, D, N);
+          for (int u = 0; u < kGatherBatch; ++u) {
+            const int32_t leaf = j0 + u < k2 ? leaves[j0 + u] : -1;
+            ok[u] = leaf >= 0 && leaf < N;
+            if (ok[u]) rows[u] = load_stream<V>(base + static_cast<int64_t>(leaf) * D);
+            if (leaf >= N && v == 0 && f0 == 0) flag_status(FSA_STATUS_BAD_NEIGHBOR);
+          }
 #pragma unroll
-        for (int c = 0; c < V; ++c) acc.v[c] = acc.v[c] / denom;
-        store_vec(slot_mean + v * V, acc);
-      }
-    }
-    if (lane == 0) a.mvalid[w] = valid;
-    __threadfence();
-    __syncwarp();
-    unsigned int prev = 0;
-    if (lane == 0) prev = atomicAdd(a.done + b, 1u);
-    prev = __shfl_sync(0xffffffffU, prev, 0);
-    if (prev != static_cast<unsigned int>(k1 - 1)) continue;
-    // ---- last slot of root b: ordered sum of the slot means ---------------
-    __threadfence();
-    const int32_t* mv = a.mvalid + b * k1;
-    int nonempty = 0;
-    for (int s = lane; s < k1; s += 32) nonempty += __ldcg(mv + s) > 0 ? 1 : 0;
+          for (int u = 0; u < kGatherBatch; ++u) {
+            if (ok[u]) {
+              ++valid;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) nonempty += __shfl_xor_sync(0xffffffffU, nonempty, o);
-    const float* means = a.inner + b * k1 * D;
-    for (int64_t v = lane; v < nv; v += 32) {
-      VecF<V> outer;
-      vzero(outer);
-      for (int s = 0; s < k1; ++s) {
-        if (__ldcg(mv + s) > 0) {
-#pragma unroll
-          for (int c = 0; c < V; ++c) outer.v[c] += __ldcg(means + s * D + v * V + c);
+              for (int c = 0; c < V; ++c) acc.v[c] += rows[u].v[c];
+            }
+          }
         }
-      }
-      if (nonempty > 0) {
-        const float denom = static_cast<float>(nonempty);
+        if (v == 0) mvalid[i] = valid;
+        if (valid > 0) {
+          const float denom = static_cast<float>(valid);
 #pragma unroll
-        for (int c = 0; c < V; ++c) outer.v[c] = outer.v[c] / denom;
-      } else {
-        vzero(outer);
+          for (int c = 0; c < V; ++c) acc.v[c] = acc.v[c] / denom;
+        }
+        store_vec(inner + i * a.dchunk + v * V, acc);
       }
-      store_vec(a.out + b * D + v * V, outer);
+      __syncthreads();
+      for (int v = tid; v < nv; v += nthreads) {
+        VecF<V> outer;
+        vzero(outer);
+        int nonempty = 0;
+        for (int i = 0; i < k1; ++i) {
+          if (mvalid[i] > 0) {
+            ++nonempty;
+            const VecF<V> m = load_vec<V>(inner + i * a.dchunk + v * V);
+#pragma unroll
+            for (int c = 0; c < V; ++c) outer.v[c] += m.v[c];
+          }
+        }
+        if (nonempty > 0) {
+          const float denom = static_cast<float>(nonempty);
+#pragma unroll
+          for (int c = 0; c < V; ++c) outer.v[c] = outer.v[c] / denom;
+        } else {
+          vzero(outer);
+        }
+        store_vec(a.out + b * D + f0 + v * V, outer);
+      }
+      __syncthreads();
     }
+    __syncthreads();
   }
 }
 
@@ -901,19 +1010,21 @@ size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 // Workspace of the 2-hop forward, in bytes from a 256-byte aligned base.
 struct Ws2 {
-  size_t pre, state, nchunks, mbeg, mtake, mdraws, next, done, mvalid, inner, s1, win2, total;
+  size_t rpre, rgroups, lpre, state, mbeg, mtake, mdraws, next, s1, win2, total;
 };
 
-Ws2 ws2_layout(int64_t B, int k1, int k2, int64_t D, bool need_s1, bool need_win2) {
+Ws2 ws2_layout(int64_t B, int k1, int k2, bool need_s1, bool need_win2) {
   Ws2 l{};
   const size_t rows = static_cast<size_t>(B) * static_cast<size_t>(k1);
   size_t off = 0;
-  l.pre = off;
-  off = align256(off + 8 * (rows + 1));
+  l.rpre = off;
+  off = align256(off + 8 * (static_cast<size_t>(B) + 1));
+  l.rgroups = off;
+  off = align256(off + 8 * static_cast<size_t>(B));
+  l.lpre = off;
+  off = align256(off + 8 * rows);
   l.state = off;
   off = align256(off + 8 * rows);
-  l.nchunks = off;
-  off = align256(off + 4 * rows);
   l.mbeg = off;
   off = align256(off + 4 * rows);
   l.mtake = off;
@@ -921,19 +1032,33 @@ Ws2 ws2_layout(int64_t B, int k1, int k2, int64_t D, bool need_s1, bool need_win
   l.mdraws = off;
   off = align256(off + 4 * rows);
   l.next = off;
-  off = align256(off + 8);
-  l.done = off;
-  off = align256(off + 4 * static_cast<size_t>(B));
-  l.mvalid = off;
-  off = align256(off + 4 * rows);
-  l.inner = off;
-  off = align256(off + 4 * rows * static_cast<size_t>(D));
+  off = align256(off + 16);
   l.s1 = off;
   if (need_s1) off = align256(off + 4 * rows);
   l.win2 = off;
   if (need_win2) off = align256(off + 4 * rows * static_cast<size_t>(k2));
   l.total = off;
   return l;
+}
+
+// Feature tile width of the gather: the per-slot means of one tile live in
+// shared memory.
+constexpr int kInnerBudgetBytes = 24 * 1024;
+constexpr int kMaxSmemBytes = 227 * 1024;
+
+bool plan_gather(int k1, int k2, int64_t D, int vec, int* dchunk_out, int* smem_out) {
+  int dchunk = 0;
+  if (D > 0) {
+    const int64_t fit = kInnerBudgetBytes / (4 * static_cast<int64_t>(k1));
+    int64_t c = fit < D ? fit : D;
+    c -= c % vec;
+    if (c < vec) c = vec;
+    dchunk = static_cast<int>(c);
+  }
+  const LayoutG l = layout_gather(k1, k2, dchunk);
+  *dchunk_out = dchunk;
+  *smem_out = l.total;
+  return l.total <= kMaxSmemBytes;
 }
 
 // Persistent grid of the draw kernel.
@@ -950,13 +1075,10 @@ int draw_grid(int* grid_out) {
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (err == cudaSuccess) {
     err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fsa_2hop_draw_kernel,
-                                                        kThreadsDraw, 0);
+                                                        kThreadsDraw, 8 * (kSmemRoots + 1));
   }
   if (err != cudaSuccess) return cuda_fail(err);
-  // One CTA per SM below full occupancy: the warps grab work dynamically, so
-  // this costs no balance, and it leaves room for the gradient zero-fill,
-  // which the autograd path runs concurrently on another stream.
-  const int grid = sms * (per_sm > 1 ? per_sm - 1 : 1);
+  const int grid = sms * (per_sm > 0 ? per_sm : 1);
   if (dev >= 0 && dev < 64) cached[dev] = grid;
   *grid_out = grid;
   return FSA_OK;
@@ -1023,11 +1145,10 @@ int fsa_sample_agg_backward(const int32_t* samples, const int32_t* takes,
 }
 
 size_t fsa_sample_agg_2hop_workspace_size(int64_t batch_size, int32_t fanout1,
-                                          int32_t fanout2, int64_t feature_dim,
-                                          int has_samples1, int has_samples2) {
-  if (batch_size <= 0 || fanout1 <= 0 || fanout2 <= 0 || feature_dim < 0) return 0;
-  return ws2_layout(batch_size, fanout1, fanout2, feature_dim, has_samples1 == 0,
-                    has_samples2 == 0).total;
+                                          int32_t fanout2, int has_samples1,
+                                          int has_samples2) {
+  if (batch_size <= 0 || fanout1 <= 0 || fanout2 <= 0) return 0;
+  return ws2_layout(batch_size, fanout1, fanout2, has_samples1 == 0, has_samples2 == 0).total;
 }
 
 int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
@@ -1038,64 +1159,83 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
                                 int32_t fanout2, uint64_t seed, float* out,
                                 int32_t* samples1, int32_t* samples2,
                                 void* workspace, size_t workspace_bytes,
+                                float* zero_fill, int64_t zero_count,
                                 void* stream) {
   if (fanout1 < 0 || fanout2 < 0 || batch_size < 0 || feature_dim < 0 ||
-      num_nodes < 0 || num_edges < 0 || batch_offset < 0) {
+      num_nodes < 0 || num_edges < 0 || batch_offset < 0 || zero_count < 0 ||
+      (zero_count > 0 && zero_fill == nullptr)) {
     return FSA_ERR_INVALID_ARGUMENT;
   }
   if (static_cast<int64_t>(fanout1) + static_cast<int64_t>(fanout1) * fanout2 >
       FSA_MAX_2HOP_ENTRIES) {
     return FSA_ERR_INVALID_ARGUMENT;
   }
-  if (batch_size == 0 || fanout1 == 0 || fanout2 == 0) return FSA_OK;
-  if (rowptr == nullptr || frontier == nullptr || (num_edges > 0 && col == nullptr) ||
-      (feature_dim > 0 && (out == nullptr || (num_nodes > 0 && x == nullptr)))) {
-    return FSA_ERR_INVALID_ARGUMENT;
-  }
-  const Ws2 wl = ws2_layout(batch_size, fanout1, fanout2, feature_dim, samples1 == nullptr,
+  const bool work = batch_size > 0 && fanout1 > 0 && fanout2 > 0;
+  const Ws2 wl = ws2_layout(batch_size, fanout1, fanout2, samples1 == nullptr,
                             samples2 == nullptr);
-  if (workspace == nullptr || workspace_bytes < wl.total || !aligned(workspace, 256)) {
+  if (work && (rowptr == nullptr || frontier == nullptr || (num_edges > 0 && col == nullptr) ||
+               (feature_dim > 0 && (out == nullptr || (num_nodes > 0 && x == nullptr))) ||
+               workspace == nullptr || workspace_bytes < wl.total || !aligned(workspace, 256))) {
     return FSA_ERR_INVALID_ARGUMENT;
   }
-  const int vec = pick_vec(feature_dim, x, out);
+  // The zero fill rides along in the draw kernel (float4 stores); a buffer
+  // that is not 16-byte aligned or has a count % 4 tail, or a call with no
+  // sampling work, gets the plain fill.
+  float4* fill4 = nullptr;
+  int64_t fill_vec4 = 0;
+  if (zero_count > 0) {
+    if (work && aligned(zero_fill, 16) && (zero_count & 3) == 0) {
+      fill4 = reinterpret_cast<float4*>(zero_fill);
+      fill_vec4 = zero_count >> 2;
+    } else {
+      const int st0 = fsa_fill_zero_f32(zero_fill, zero_count, stream);
+      if (st0 != FSA_OK) return st0;
+    }
+  }
+  if (!work) return FSA_OK;
+  int vec = pick_vec(feature_dim, x, out);
+  int dchunk = 0, gsmem = 0;
+  while (!plan_gather(fanout1, fanout2, feature_dim, vec, &dchunk, &gsmem)) {
+    if (vec == 1) return FSA_ERR_INVALID_ARGUMENT;
+    vec >>= 1;
+  }
   char* ws = static_cast<char*>(workspace);
   int32_t* s1 = samples1 != nullptr ? samples1 : reinterpret_cast<int32_t*>(ws + wl.s1);
   int32_t* win2 = samples2 != nullptr ? samples2 : reinterpret_cast<int32_t*>(ws + wl.win2);
-  auto* pre = reinterpret_cast<long long*>(ws + wl.pre);
+  auto* rpre = reinterpret_cast<long long*>(ws + wl.rpre);
+  auto* rgroups = reinterpret_cast<long long*>(ws + wl.rgroups);
+  auto* lpre = reinterpret_cast<long long*>(ws + wl.lpre);
   auto* state = reinterpret_cast<unsigned long long*>(ws + wl.state);
-  auto* nchunks = reinterpret_cast<int32_t*>(ws + wl.nchunks);
   auto* mbeg = reinterpret_cast<int32_t*>(ws + wl.mbeg);
   auto* mtake = reinterpret_cast<int32_t*>(ws + wl.mtake);
   auto* mdraws = reinterpret_cast<int32_t*>(ws + wl.mdraws);
   auto* next = reinterpret_cast<unsigned long long*>(ws + wl.next);
-  auto* done = reinterpret_cast<unsigned int*>(ws + wl.done);
-  auto* mvalid = reinterpret_cast<int32_t*>(ws + wl.mvalid);
-  auto* inner = reinterpret_cast<float*>(ws + wl.inner);
   auto s = static_cast<cudaStream_t>(stream);
-  const int64_t rows = batch_size * fanout1;
 
   const Plan2Args pa{rowptr, col, num_nodes, num_edges, frontier, batch_size, batch_offset,
-                     fanout1, fanout2, seed, s1, win2, mbeg, mtake, mdraws, nchunks, state,
-                     done, next};
-  int st = launch(fsa_2hop_plan_kernel, grid_for(batch_size), kThreadsPlan, 4 * fanout1, s, pa);
+                     fanout1, fanout2, seed, s1, win2, mbeg, mtake, mdraws, state, lpre,
+                     rgroups, next};
+  const int psmem = ((4 * fanout1 + 15) & ~15) + 8 * fanout1;
+  int st = launch(fsa_2hop_plan_kernel, grid_for(batch_size), kThreadsPlan, psmem, s, pa);
   if (st != FSA_OK) return st;
-  const Scan2Args sa{nchunks, pre, rows};
+  const Scan2Args sa{rgroups, rpre, batch_size};
   st = launch(fsa_2hop_scan_kernel, 1, kThreadsScan, 0, s, sa);
   if (st != FSA_OK) return st;
   int dgrid = 0;
   st = draw_grid(&dgrid);
   if (st != FSA_OK) return st;
-  const Draw2Args da{pre, state, mtake, mdraws, rows, fanout2, win2, next};
-  st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, 0, s, da);
+  const Draw2Args da{rpre, lpre, state, mtake, mdraws, batch_size, fanout1, fanout2, win2,
+                     next, fill4, fill_vec4, kSmemRoots};
+  const int dsmem = batch_size < kSmemRoots ? static_cast<int>(8 * (batch_size + 1)) : 0;
+  st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st != FSA_OK) return st;
   const Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
-                       mtake, win2, inner, mvalid, done, out};
-  const int64_t warps_per_cta = kThreadsGather / 32;
-  const int ggrid = grid_for((batch_size * fanout1 + warps_per_cta - 1) / warps_per_cta);
+                       mtake, win2, samples2, out, dchunk};
+  const int ggrid = grid_for(batch_size);
   switch (vec) {
-    case 4: return launch(fsa_2hop_gather_kernel<4>, ggrid, kThreadsGather, 0, s, ga);
-    case 2: return launch(fsa_2hop_gather_kernel<2>, ggrid, kThreadsGather, 0, s, ga);
-    default: return launch(fsa_2hop_gather_kernel<1>, ggrid, kThreadsGather, 0, s, ga);
+    case 4: return launch(fsa_2hop_gather_kernel<4>, ggrid, kThreadsGather, gsmem, s, ga);
+    case 2: return launch(fsa_2hop_gather_kernel<2>, ggrid, kThreadsGather, gsmem, s, ga);
+    default: return launch(fsa_2hop_gather_kernel<1>, ggrid, kThreadsGather, gsmem, s, ga);
   }
 }
 

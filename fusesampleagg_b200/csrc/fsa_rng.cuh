@@ -111,8 +111,9 @@ constexpr JumpTables make_jump_tables() {
 // step 2^kChunkLog2 (one chunk) and one for 32 chunks, the start state of
 // chunk j of a row is  K1[j % 32] * K2[(j / 32) % 32] * T^(...) s0: one or
 // two table products per lane, plus one jump matrix per set bit of j / 1024
-// (rows of more than 2^(kChunkLog2 + 10) draws only).
-constexpr int kChunkLog2 = 5;
+// (rows of more than 2^(kChunkLog2 + 10) draws only).  64-draw chunks were
+// the fastest of 32/64/128 on the 2-hop power-law workload.
+constexpr int kChunkLog2 = 6;
 constexpr int kLaneTables = 32;
 
 struct LaneTables {

@@ -89,15 +89,23 @@ FSA_API int fsa_sample_agg_backward(const int32_t* samples, const int32_t* takes
  * are optional (NULL = not written).
  *
  * Unlike the reference launcher this one needs a device workspace (the
- * second-hop row table, chunk prefixes, per-slot means, plus the id
- * buffers that are not requested as outputs): at least
+ * second-hop row table, per-row initial states and draw-group prefixes,
+ * plus the id buffers that are not requested as outputs): at least
  * fsa_sample_agg_2hop_workspace_size(...) bytes, 256-byte aligned, owned by
  * the caller and not used by anything else until the call's work on `stream`
  * has finished.  Its contents need no initialisation.
+ *
+ * zero_fill / zero_count (optional, NULL / 0 = none): a float buffer to set
+ * to zero as part of the call -- typically the dense feature gradient the
+ * backward will scatter into (what the reference allocates with at::zeros,
+ * fuseop/binding.cpp:220).  The sampling kernel is bound by integer issue
+ * and the fill by HBM writes, so the fill is interleaved into it and costs
+ * little extra time.  The buffer is zero when the call's work on `stream`
+ * has finished.
  */
 FSA_API size_t fsa_sample_agg_2hop_workspace_size(int64_t batch_size, int32_t fanout1,
-                                                  int32_t fanout2, int64_t feature_dim,
-                                                  int has_samples1, int has_samples2);
+                                                  int32_t fanout2, int has_samples1,
+                                                  int has_samples2);
 
 FSA_API int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
                                         int64_t num_nodes, int64_t num_edges,
@@ -107,6 +115,7 @@ FSA_API int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* co
                                         int32_t fanout2, uint64_t seed, float* out,
                                         int32_t* samples1, int32_t* samples2,
                                         void* workspace, size_t workspace_bytes,
+                                        float* zero_fill, int64_t zero_count,
                                         void* stream);
 
 /*

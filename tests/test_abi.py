@@ -66,7 +66,8 @@ def test_zero_sized_calls_are_noops_without_cuda():
     assert L.fsa_sample_agg_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, 0, 0, 1,
                                     NULL, NULL, NULL, NULL) == _lib.FSA_OK
     assert L.fsa_sample_agg_2hop_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, 0, 0, 3, 1,
-                                         NULL, NULL, NULL, NULL, 0, NULL) == _lib.FSA_OK
+                                         NULL, NULL, NULL, NULL, 0, NULL, 0,
+                                         NULL) == _lib.FSA_OK
     assert L.fsa_sample_agg_2hop_backward(NULL, NULL, NULL, 0, 4, 3, 2, NULL, 10,
                                           NULL) == _lib.FSA_OK
     assert L.fsa_fill_zero_f32(NULL, 0, NULL) == _lib.FSA_OK
@@ -75,7 +76,7 @@ def test_zero_sized_calls_are_noops_without_cuda():
 @pytest.mark.parametrize("f1,f2", [(-1, 2), (2, -1), (12000, 1), (1000, 12)])
 def test_2hop_rejects_bad_fanouts(f1, f2):
     assert L.fsa_sample_agg_2hop_forward(NULL, NULL, 10, 10, NULL, 4, NULL, 5, 0, f1, f2, 1,
-                                         NULL, NULL, NULL, NULL, 0,
+                                         NULL, NULL, NULL, NULL, 0, NULL, 0,
                                          NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
     assert L.fsa_sample_agg_2hop_backward(NULL, NULL, NULL, 5, 4, f1, f2, NULL, 10,
                                           NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
@@ -98,12 +99,10 @@ def test_negative_sizes_rejected():
 
 
 def test_workspace_size():
-    assert L.fsa_sample_agg_2hop_workspace_size(0, 15, 10, 100, 0, 0) == 0
-    assert L.fsa_sample_agg_2hop_workspace_size(8, 0, 10, 100, 0, 0) == 0
-    with_ids = L.fsa_sample_agg_2hop_workspace_size(1024, 15, 10, 100, 1, 1)
-    without = L.fsa_sample_agg_2hop_workspace_size(1024, 15, 10, 100, 0, 0)
-    # per-slot means are part of the workspace
-    assert with_ids >= 4 * 1024 * 15 * 100
+    assert L.fsa_sample_agg_2hop_workspace_size(0, 15, 10, 0, 0) == 0
+    assert L.fsa_sample_agg_2hop_workspace_size(8, 0, 10, 0, 0) == 0
+    with_ids = L.fsa_sample_agg_2hop_workspace_size(1024, 15, 10, 1, 1)
+    without = L.fsa_sample_agg_2hop_workspace_size(1024, 15, 10, 0, 0)
     assert 0 < with_ids < without
     assert with_ids % 256 == 0 and without % 256 == 0
     # without requested ids the workspace also holds samples1 and samples2
@@ -112,12 +111,15 @@ def test_workspace_size():
 
 def test_2hop_forward_rejects_small_workspace():
     args = (1, 1, 10, 10, 1, 4, 1, 5, 0, 3, 2, 1, 1, NULL, NULL)
-    need = L.fsa_sample_agg_2hop_workspace_size(5, 3, 2, 4, 0, 0)
-    assert L.fsa_sample_agg_2hop_forward(*args, 256, need - 1,
+    need = L.fsa_sample_agg_2hop_workspace_size(5, 3, 2, 0, 0)
+    assert L.fsa_sample_agg_2hop_forward(*args, 256, need - 1, NULL, 0,
                                          NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
-    assert L.fsa_sample_agg_2hop_forward(*args, 8, need,
+    assert L.fsa_sample_agg_2hop_forward(*args, 8, need, NULL, 0,
                                          NULL) == _lib.FSA_ERR_INVALID_ARGUMENT  # misaligned
-    assert L.fsa_sample_agg_2hop_forward(*args, NULL, need,
+    assert L.fsa_sample_agg_2hop_forward(*args, NULL, need, NULL, 0,
+                                         NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    # a zero-fill request needs a buffer
+    assert L.fsa_sample_agg_2hop_forward(*args, 256, need, NULL, 16,
                                          NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
 
 

@@ -80,7 +80,7 @@ def test_row_seeds_match_oracle(run):
 
 def test_chunk_start_equals_serial_steps(run):
     rng = random.Random(5)
-    chunk = 32
+    chunk = 64
     js = [0, 1, 2, 5, 31, 32, 33, 63, 64, 65, 100, 127, 128, 500, 1023, 1024, 1025, 4097,
           33_000, 16_000_000 // chunk]
     cases = [(rng.getrandbits(64) | 1, j) for j in js]
