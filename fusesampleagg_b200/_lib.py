@@ -51,7 +51,7 @@ SIGNATURES = {
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
-            f"{LIB_PATH.name} is not built; run `python -m fusesampleagg_b200.build` "
+            f"{LIB_PATH.name} is not built; run `python fusesampleagg_b200/build.py` "
             "(nvcc with sm_100a) before importing fusesampleagg_b200"
         )
     try:

@@ -5,7 +5,8 @@ the CUDA runtime statically, so it loads into any process (including one
 without a GPU, for symbol checks) and shares the device's primary context
 with PyTorch.
 
-Usage: ``python -m fusesampleagg_b200.build [--force] [--verbose]``.
+Usage: ``python fusesampleagg_b200/build.py [--force] [--verbose]`` (run as a
+script: importing the package loads the library this builds).
 """
 
 from __future__ import annotations
