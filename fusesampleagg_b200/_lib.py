@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libfsa_sm100.so"
 FSA_OK = 0
 FSA_ERR_INVALID_ARGUMENT = 1
 FSA_ERR_CUDA = 2
+FSA_ERR_SCRATCH_LIMIT = 3
 
 FSA_STATUS_BAD_ROOT = 0x1
 FSA_STATUS_BAD_ROW = 0x2
@@ -21,6 +22,7 @@ FSA_STATUS_BAD_NEIGHBOR = 0x4
 
 MAX_FANOUT_1HOP = 1024
 MAX_2HOP_ENTRIES = 12000
+NOALLOC_SCRATCH_BYTES = 4194304
 
 # Every symbol include/fsa_sm100.h declares, with (restype, argtypes).
 _p = ctypes.c_void_p
@@ -38,6 +40,9 @@ SIGNATURES = {
     "fsa_sample_agg_2hop_forward": (
         _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p,
                _p, ctypes.c_size_t, _p, _i64, _p]),
+    "fsa_sample_agg_2hop_forward_noalloc": (
+        _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p,
+               _p, _i64, _p]),
     "fsa_sample_agg_2hop_backward": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),

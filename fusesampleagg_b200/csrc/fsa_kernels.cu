@@ -1297,6 +1297,9 @@ const char* fsa_status_string(int status) {
     case FSA_OK: return "ok";
     case FSA_ERR_INVALID_ARGUMENT: return "invalid argument";
     case FSA_ERR_CUDA: return "CUDA runtime error";
+    case FSA_ERR_SCRATCH_LIMIT:
+      return "batch needs more than the library's static scratch "
+             "(FSA_NOALLOC_SCRATCH_BYTES); use the workspace entry point";
     default: return "unknown status";
   }
 }
@@ -1324,6 +1327,87 @@ int fsa_device_status(int device, uint32_t* flags, int reset) {
   if (err2 != cudaSuccess) return cuda_fail(err2);
   *flags = v;
   return FSA_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// 2-hop forward on library-owned scratch (no counterpart in the reference)
+// ---------------------------------------------------------------------------
+
+// Module-scope scratch for fsa_sample_agg_2hop_forward_noalloc: one copy per
+// device, reserved when the module is loaded on that device, never freed.
+static __device__ __align__(256) unsigned char g_ws2_scratch[FSA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kScratchDevices = 256;
+std::atomic<void*> g_scratch_addr[kScratchDevices];
+
+// Device address of g_ws2_scratch on the current device.  The first call
+// per device runs cudaGetSymbolAddress (which also loads the module there);
+// later calls read the cached pointer.
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  const bool cached = dev >= 0 && dev < kScratchDevices;
+  if (cached) {
+    void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
+    if (p != nullptr) {
+      *out = p;
+      return FSA_OK;
+    }
+  }
+  void* p = nullptr;
+  err = cudaGetSymbolAddress(&p, g_ws2_scratch);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (p == nullptr) return FSA_ERR_CUDA;
+  if (cached) g_scratch_addr[dev].store(p, std::memory_order_release);
+  *out = p;
+  return FSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fsa_sample_agg_2hop_forward_noalloc(const int32_t* rowptr, const int32_t* col,
+                                        int64_t num_nodes, int64_t num_edges,
+                                        const float* x, int64_t feature_dim,
+                                        const int32_t* frontier, int64_t batch_size,
+                                        int64_t batch_offset, int32_t fanout1,
+                                        int32_t fanout2, uint64_t seed, float* out,
+                                        int32_t* samples1, int32_t* samples2,
+                                        float* zero_fill, int64_t zero_count,
+                                        void* stream) {
+  const bool work = batch_size > 0 && fanout1 > 0 && fanout2 > 0 &&
+                    static_cast<int64_t>(fanout1) + static_cast<int64_t>(fanout1) * fanout2 <=
+                        FSA_MAX_2HOP_ENTRIES;
+  if (!work) {
+    // Nothing to sample (or arguments the workspace entry point rejects):
+    // no scratch is used.
+    return fsa_sample_agg_2hop_forward(rowptr, col, num_nodes, num_edges, x, feature_dim,
+                                       frontier, batch_size, batch_offset, fanout1, fanout2,
+                                       seed, out, samples1, samples2, nullptr, 0, zero_fill,
+                                       zero_count, stream);
+  }
+  // Size limit first, before any CUDA call.  A batch with more roots than
+  // scratch bytes cannot fit (8 bytes per root alone); checking that first
+  // keeps the layout arithmetic far from overflow.
+  if (batch_size > static_cast<int64_t>(FSA_NOALLOC_SCRATCH_BYTES) ||
+      ws2_layout(batch_size, fanout1, fanout2, samples1 == nullptr, samples2 == nullptr).total >
+          static_cast<size_t>(FSA_NOALLOC_SCRATCH_BYTES)) {
+    return FSA_ERR_SCRATCH_LIMIT;
+  }
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != FSA_OK) return st;
+  return fsa_sample_agg_2hop_forward(rowptr, col, num_nodes, num_edges, x, feature_dim,
+                                     frontier, batch_size, batch_offset, fanout1, fanout2, seed,
+                                     out, samples1, samples2, scratch,
+                                     static_cast<size_t>(FSA_NOALLOC_SCRATCH_BYTES), zero_fill,
+                                     zero_count, stream);
 }
 
 }  // extern "C"

@@ -41,10 +41,12 @@ extern "C" {
 #define FSA_OK 0
 #define FSA_ERR_INVALID_ARGUMENT 1 /* a size / fanout / pointer check failed */
 #define FSA_ERR_CUDA 2             /* a CUDA runtime call failed; see fsa_last_cuda_error */
+#define FSA_ERR_SCRATCH_LIMIT 3    /* call too large for FSA_NOALLOC_SCRATCH_BYTES */
 
 /* Limits, same values as the reference (fuseop/binding.cpp:13-14). */
 #define FSA_MAX_FANOUT_1HOP 1024
 #define FSA_MAX_2HOP_ENTRIES 12000 /* fanout1 + fanout1 * fanout2 */
+#define FSA_NOALLOC_SCRATCH_BYTES 4194304 /* scratch of the _noalloc entry point */
 
 /* Bits of the per-device status word (fsa_device_status). */
 #define FSA_STATUS_BAD_ROOT 0x1u     /* frontier id outside [0, num_nodes) */
@@ -117,6 +119,48 @@ FSA_API int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* co
                                         void* workspace, size_t workspace_bytes,
                                         float* zero_fill, int64_t zero_count,
                                         void* stream);
+
+/*
+ * 2-hop forward on library-owned scratch.  No counterpart in the reference:
+ * the reference launcher (fuseop/fused_sample_agg.cu:303-315) needs no
+ * scratch, and the workspace entry point above takes it from the caller.
+ *
+ * Same arguments and results as fsa_sample_agg_2hop_forward, without
+ * workspace / workspace_bytes.  For callers that cannot allocate device
+ * memory at call time: a C / cgo / JNI host that holds only raw device
+ * pointers handed over by another runtime and no allocator of its own, or a
+ * serving loop that must not call cudaMalloc / cudaFree (both synchronise
+ * the whole device) nor route through a framework allocator.  The call
+ * allocates nothing; its scratch is a static device array of
+ * FSA_NOALLOC_SCRATCH_BYTES (4 MiB) per device, reserved when the library's
+ * device code is loaded on that device.
+ *
+ * Limit: fsa_sample_agg_2hop_workspace_size(batch_size, fanout1, fanout2,
+ * samples1 != NULL, samples2 != NULL) must not exceed
+ * FSA_NOALLOC_SCRATCH_BYTES, else the call returns FSA_ERR_SCRATCH_LIMIT
+ * before any CUDA call.  That covers 1,024 roots at fanouts 15 x 10 (about
+ * 1.1 MB without caller id buffers) and up to about 9,500 roots at 15 x 10
+ * when samples1 and samples2 are given.
+ *
+ * The first call on a device does set-up: cudaGetSymbolAddress of the
+ * scratch (which loads the module on that device if needed), checked and
+ * then cached per device.  Make that first call before any stream capture.
+ * Nothing in the scratch needs to start at zero: the call's first kernel
+ * writes every word the later kernels read.
+ *
+ * All calls on one device share the one scratch array, so calls whose work
+ * overlaps on the device race and give wrong results: issue them on one
+ * stream, or order them with events.
+ */
+FSA_API int fsa_sample_agg_2hop_forward_noalloc(const int32_t* rowptr, const int32_t* col,
+                                                int64_t num_nodes, int64_t num_edges,
+                                                const float* x, int64_t feature_dim,
+                                                const int32_t* frontier, int64_t batch_size,
+                                                int64_t batch_offset, int32_t fanout1,
+                                                int32_t fanout2, uint64_t seed, float* out,
+                                                int32_t* samples1, int32_t* samples2,
+                                                float* zero_fill, int64_t zero_count,
+                                                void* stream);
 
 /*
  * 2-hop backward (saved-index replay).  Replaces
