@@ -215,7 +215,9 @@ def byte_model(w, inp: Inputs, batches: list[int]) -> dict:
 
     k1, k2 = w.fanouts
     B, D = inp.B, w.dim
-    tot = {"fwd": 0.0, "bwd": 0.0, "unique_leaf_rows": 0.0, "valid_leaves": 0.0}
+    tot = {"fwd": 0.0, "bwd": 0.0, "unique_leaf_rows": 0.0, "valid_leaves": 0.0,
+           "rng_draws": 0.0}
+    deg = (inp.rowptr[1:] - inp.rowptr[:-1]).long()
     with torch.no_grad():
         for i in batches:
             _, s1, s2 = fsa.fused_sample_agg_2hop_with_samples(
@@ -228,6 +230,11 @@ def byte_model(w, inp: Inputs, batches: list[int]) -> dict:
             fwd = (4 * B + 8 * (B + valid_mid) + 4 * (take1 + valid_leaves)
                    + 4 * D * valid_leaves + 4 * D * B + saved)
             bwd = 4 * D * B + saved + 8 * D * valid_leaves
+            # Reservoir draws (one xorshift64* output each) past the first
+            # `fanout` positions of every sampled row: the sampler's work.
+            mids = s1[s1 >= 0].long()
+            tot["rng_draws"] += float((deg[inp.frontiers[i].long()] - k1).clamp_min(0).sum()
+                                      + (deg[mids] - k2).clamp_min(0).sum())
             leaves = s2[s2 >= 0]
             tot["fwd"] += fwd
             tot["bwd"] += bwd
@@ -528,6 +535,7 @@ def run(args) -> None:
         }
         result["kernels"] = kernels
         result["unique_leaf_rows_per_batch"] = bytes_model["unique_leaf_rows"]
+        result["rng_draws_per_batch"] = bytes_model["rng_draws"]
         result["gpu_launches"] = launches
         if dist.rank == 0 and world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(w, inp, budget_s=args.cpu_budget)

@@ -64,6 +64,8 @@ __device__ __forceinline__ void flag_status(unsigned int bits) {
 
 __device__ constexpr fsa::LaneTables g_lanes1 = fsa::make_lane_tables(fsa::kChunkLog2);
 __device__ constexpr fsa::LaneTables g_lanes2 = fsa::make_lane_tables(fsa::kChunkLog2 + 5);
+__device__ constexpr fsa::LaneTablesT g_lanes1_t =
+    fsa::transpose_lane_tables(fsa::make_lane_tables(fsa::kChunkLog2));
 
 constexpr uint32_t kChunk = 1u << fsa::kChunkLog2;
 constexpr uint32_t kStarMulLo = static_cast<uint32_t>(fsa::kStarMul);
@@ -363,12 +365,13 @@ __global__ void __launch_bounds__(kThreads1Hop)
 
 constexpr int kThreadsPlan = 128;
 constexpr int kThreadsScan = 1024;
-constexpr int kThreadsDraw = 256;
+constexpr int kThreadsDraw = 768;
 constexpr int kThreadsGather = 256;
 
-// Draws of a second-hop row are processed in groups of 32 chunks (one chunk
-// per lane, kGroupDraws draws); a warp takes one group at a time.
-constexpr uint32_t kGroupDraws = 32u * kChunk;
+// Draws of a second-hop row are split into chunks of kChunk positions; the
+// chunks of all rows are numbered consecutively (roots in batch order, their
+// rows in slot order, each row's chunks in position order) and a warp takes
+// 32 consecutive chunks at a time, one per lane, whichever rows they are in.
 
 struct Plan2Args {
   const int32_t* rowptr;
@@ -387,8 +390,8 @@ struct Plan2Args {
   int32_t* mtake;            // [R] reservoir size of each second-hop row
   int32_t* mdraws;           // [R] draws of each second-hop row
   unsigned long long* state; // [R] initial xorshift state of each second-hop row
-  long long* lpre;           // [R] group prefix of the row within its root
-  long long* rgroups;        // [B] groups of all second-hop rows of a root
+  long long* lpre;           // [R] chunk prefix of the row within its root
+  long long* rgroups;        // [B] chunks of all second-hop rows of a root
   unsigned long long* next;  // draw-kernel fill-block counter, reset here
 };
 
@@ -402,7 +405,7 @@ __global__ void __launch_bounds__(kThreadsPlan)
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
   const int64_t N = a.num_nodes;
-  if (blockIdx.x == 0 && tid == 0) *a.next = 0;
+  if (blockIdx.x == 0 && tid == 0) *a.next = 0;  // fill-block counter of the draw kernel
 
   for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
     const int32_t root = a.frontier[b];
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(kThreadsPlan)
       a.mtake[r] = mt;
       a.mdraws[r] = md - mt;
       a.state[r] = fsa::row_state(a.seed, static_cast<uint64_t>(root), 1, static_cast<uint64_t>(i));
-      groups[i] = (static_cast<long long>(md - mt) + kGroupDraws - 1) / kGroupDraws;
+      groups[i] = (static_cast<long long>(md - mt) + kChunk - 1) / kChunk;
     }
     // Every second-hop slot starts as "kept" (no winner).
     for (int64_t e = tid; e < static_cast<int64_t>(k1) * k2; e += nthreads) {
@@ -525,8 +528,8 @@ __global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2
 }
 
 struct Draw2Args {
-  const long long* rpre;             // [B + 1] group prefix over roots
-  const long long* lpre;             // [R] group prefix of each row within its root
+  const long long* rpre;             // [B + 1] chunk prefix over roots
+  const long long* lpre;             // [R] chunk prefix of each row within its root
   const unsigned long long* state;   // [R]
   const int32_t* mtake;              // [R]
   const int32_t* mdraws;             // [R]
@@ -540,139 +543,146 @@ struct Draw2Args {
   int smem_roots;                    // rpre staged in shared memory when B < this
 };
 
-// Fill work item: kFillItemVec4 float4 stores per lane (32 KB per warp); a
-// warp takes up to kFillPerGroup of them after each draw group.
+// Fill work item: kFillItemVec4 float4 stores per lane (32 KB per warp).
+// The first kFillWarps warps of every CTA zero the buffer while the other
+// warps draw.
 constexpr int kFillItemVec4 = 64;
-constexpr int kFillPerGroup = 2;
-constexpr int kSmemRoots = 4096;
+constexpr int kFillWarps = 4;
+constexpr int kSmemRoots = 2048;
+constexpr int kDrawTableBytes = static_cast<int>(sizeof(fsa::LaneTablesT));  // 64 KB
+
+// Zeroes fill block `idx` (32 KB) with streaming stores.  A full block is
+// 64 stores per lane at immediate offsets from one address: the draws share
+// the integer pipe with this loop, so it does no per-store arithmetic.
+__device__ __forceinline__ void fill_block(float4* fill, int64_t fill_vec4, long long idx,
+                                           int lane) {
+  const long long v0 = idx * 32LL * kFillItemVec4;
+  const float4 z = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+  float4* p = fill + v0 + lane;
+  if (v0 + 32LL * kFillItemVec4 <= fill_vec4) {
+#pragma unroll
+    for (int k = 0; k < kFillItemVec4; ++k) __stcs(p + 32 * k, z);
+  } else {
+    for (long long v = v0 + lane; v < fill_vec4; v += 32) __stcs(fill + v, z);
+  }
+}
+
+// Claims the next work item of counter `c` for the warp (lane 0 adds, the
+// value is broadcast).  All 32 lanes must call it.
+__device__ __forceinline__ long long claim(unsigned long long* c, int lane) {
+  unsigned long long v = 0;
+  if (lane == 0) v = atomicAdd(c, 1ULL);
+  return static_cast<long long>(__shfl_sync(0xffffffffU, v, 0));
+}
 
 // Largest idx in [0, n) with arr[idx] <= key, given arr[0] <= key and arr
-// non-decreasing: a 32-way search, one probe per lane per round.  Must be
-// called by all 32 lanes with the same arguments.
-__device__ __forceinline__ int64_t warp_search(const long long* arr, int64_t n, long long key,
-                                               int lane) {
+// non-decreasing (one thread).
+__device__ __forceinline__ int64_t upper_index(const long long* arr, int64_t n, long long key) {
   int64_t lo = 0, hi = n - 1;
   while (hi > lo) {
-    const int64_t step = (hi - lo + 32) / 32;
-    const int64_t idx = lo + lane * step;
-    const bool ok = idx <= hi && arr[idx] <= key;
-    const unsigned m = __ballot_sync(0xffffffffU, ok);
-    const int k = 31 - __clz(m);
-    lo += k * step;
-    hi = min(hi, lo + step - 1);
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (arr[mid] <= key) {
+      lo = mid;
+    } else {
+      hi = mid - 1;
+    }
   }
   return lo;
 }
 
-// Zeroes fill block `idx` (32 KB) with streaming stores.
-__device__ __forceinline__ void fill_block(float4* fill, int64_t fill_vec4, long long idx,
-                                           int lane) {
-  const long long v0 = idx * 32LL * kFillItemVec4 + lane;
-  const float4 z = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
-#pragma unroll 8
-  for (int k = 0; k < kFillItemVec4; ++k) {
-    const long long v = v0 + 32LL * k;
-    if (v < fill_vec4) __stcs(fill + v, z);
+// Draws of global chunk c (one thread): the root and the row are found in
+// the two prefix levels, the chunk's start state is two table products of
+// the row's initial state (plus one per set bit of j / 1024 for very long
+// rows).
+__device__ __forceinline__ void draw_chunk(const Draw2Args& a, const long long* rpre,
+                                           const uint64_t* k1, long long c) {
+  const int f1 = a.fanout1;
+  const int64_t b = upper_index(rpre, a.batch_size, c);
+  const long long local = c - rpre[b];
+  const int i = static_cast<int>(upper_index(a.lpre + b * f1, f1, local));
+  const int64_t r = b * f1 + i;
+  const uint32_t j = static_cast<uint32_t>(local - __ldg(a.lpre + r));
+  const uint32_t take = static_cast<uint32_t>(__ldg(a.mtake + r));
+  const uint32_t nd = static_cast<uint32_t>(__ldg(a.mdraws + r));
+  const uint64_t s0 = __ldg(a.state + r);
+  const uint32_t off = j * kChunk;
+  // T^(j * kChunk) s0: the (j mod 32)-chunk part from the shared copy of the
+  // one-chunk lane tables, the rest from global tables that the lanes of a
+  // warp mostly share.
+  uint64_t st = 0;
+  {
+    const uint64_t* tab = k1 + (j & 31);
+#pragma unroll
+    for (int p = 0; p < 16; ++p) st ^= tab[(p * 16 + static_cast<int>((s0 >> (4 * p)) & 15)) * 32];
   }
+  if ((j >> 5) & 31) st = apply_table(&g_lanes2.v[(j >> 5) & 31][0][0], st);
+  uint32_t hi = j >> 10;
+#pragma unroll 1
+  while (hi != 0) {
+    const int bit = __ffs(hi) - 1;
+    hi &= hi - 1;
+    st = apply_table(&g_jump.v[fsa::kChunkLog2 + 10 + bit][0][0], st);
+  }
+  chunk_draws(st, take + off, nd - off < kChunk ? nd - off : kChunk, take,
+              a.win2 + r * a.fanout2);
 }
 
-// Persistent grid.  Warp w draws groups w, w + W, w + 2W, ... of the global
-// group sequence (roots in batch order, their second-hop rows in slot order,
-// each row's groups in position order); the per-group set-up is a few
-// dependent loads: the root is found in a shared-memory copy of the root
-// prefix, the root's row descriptors are read lane-parallel in one round,
-// the group's part of the jump is one broadcast table product and the
-// lane's part one more.  Lane l of group g of a row runs chunk 32 g + l.
+// Persistent grid, two CTAs of 24 warps per SM.  Each CTA keeps a shared
+// copy of the one-chunk lane tables (64 KB, lane index innermost) and of
+// the root prefix.  Lane l of group G draws global chunk 32 G + l: two
+// binary searches find its root and row, and its start state is one
+// shared-table product plus one global-table product that the warp's lanes
+// mostly share.
 //
-// Optionally the warps also zero a buffer (the backward's dense gradient)
-// in 32 KB blocks taken from a shared counter between draw groups: the draw
-// loop is bound by integer issue, the fill by HBM writes.
-__global__ void __launch_bounds__(kThreadsDraw) fsa_2hop_draw_kernel(const Draw2Args a) {
+// Optionally the kernel also zeroes a buffer (the backward's dense
+// gradient) in 32 KB blocks claimed from the counter next[0], which the
+// plan kernel resets.  The draw loop is bound by integer issue, the fill by
+// HBM writes, so they run side by side in different warps: the first
+// kFillWarps warps of each CTA fill, the other warps draw and then help
+// with what is left of the fill.  (Warps that alternated between the two
+// would tie each one's progress to the other's.)
+__global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Draw2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  long long* s_rpre = reinterpret_cast<long long*>(smem_raw);  // [B + 1] when staged
+  uint64_t* s_k1 = reinterpret_cast<uint64_t*>(smem_raw);  // one-chunk lane tables, [p][nib][l]
+  long long* s_rpre = reinterpret_cast<long long*>(smem_raw + kDrawTableBytes);  // [B + 1]
   const int lane = threadIdx.x & 31;
   const int64_t B = a.batch_size;
-  const int k1 = a.fanout1;
-  const int k2 = a.fanout2;
   const bool staged = B < a.smem_roots;
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(&g_lanes1_t.v[0][0][0]);
+    uint4* dst = reinterpret_cast<uint4*>(s_k1);
+    for (int t = threadIdx.x; t < kDrawTableBytes / 16; t += blockDim.x) dst[t] = __ldg(src + t);
+  }
   if (staged) {
     for (int64_t t = threadIdx.x; t <= B; t += blockDim.x) s_rpre[t] = __ldg(a.rpre + t);
   }
   __syncthreads();
-  const long long total = staged ? s_rpre[B] : __ldg(a.rpre + B);
+  const long long* rpre = staged ? s_rpre : a.rpre;
+  const long long total = rpre[B];
   const long long nfill = (a.fill_vec4 + 32LL * kFillItemVec4 - 1) / (32LL * kFillItemVec4);
-  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  bool fill_left = nfill > 0;
-
-  for (long long G = warp_id; G < total; G += nwarps) {
-    const int64_t b = staged ? warp_search(s_rpre, B, G, lane) : warp_search(a.rpre, B, G, lane);
-    const long long local = G - (staged ? s_rpre[b] : __ldg(a.rpre + b));
-    // Slot within the root, and that row's fields.
-    int i;
-    uint32_t take, nd;
-    uint64_t s0;
-    long long lpi;
-    if (k1 <= 32) {
-      // One round: lane l reads row l of the root; the slot is the last row
-      // whose group prefix is <= local.
-      const int64_t rl = b * k1 + lane;
-      const bool in = lane < k1;
-      const long long lp = in ? __ldg(a.lpre + rl) : LLONG_MAX;
-      const int tk = in ? __ldg(a.mtake + rl) : 0;
-      const int dr = in ? __ldg(a.mdraws + rl) : 0;
-      const unsigned long long st = in ? __ldg(a.state + rl) : 0ULL;
-      const unsigned m = __ballot_sync(0xffffffffU, lp <= local);
-      i = 31 - __clz(m);
-      take = static_cast<uint32_t>(__shfl_sync(0xffffffffU, tk, i));
-      nd = static_cast<uint32_t>(__shfl_sync(0xffffffffU, dr, i));
-      s0 = __shfl_sync(0xffffffffU, st, i);
-      lpi = __shfl_sync(0xffffffffU, lp, i);
-    } else {
-      i = static_cast<int>(warp_search(a.lpre + b * k1, k1, local, lane));
-      const int64_t ri = b * k1 + i;
-      take = static_cast<uint32_t>(__ldg(a.mtake + ri));
-      nd = static_cast<uint32_t>(__ldg(a.mdraws + ri));
-      s0 = __ldg(a.state + ri);
-      lpi = __ldg(a.lpre + ri);
+  // With a fill, the first kFillWarps warps of every CTA zero the buffer
+  // and the others draw; without one, every warp draws.  Groups of 32
+  // chunks cost about the same, so drawing warps take them round robin.
+  const int warps = static_cast<int>(blockDim.x >> 5);
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const int fillers = nfill > 0 ? kFillWarps : 0;
+  if (warp < fillers) {
+    for (long long item = claim(a.next, lane); item < nfill; item = claim(a.next, lane)) {
+      fill_block(a.fill, a.fill_vec4, item, lane);
     }
-    const int64_t r = b * k1 + i;
-    const uint32_t g = static_cast<uint32_t>(local - lpi);
-    // Group part of the jump (warp-uniform): T^(g * kGroupDraws) s0.
-    uint64_t sg = s0;
-    if (g & 31) sg = apply_table(&g_lanes2.v[g & 31][0][0], sg);
-    uint32_t hi = g >> 5;
-#pragma unroll 1
-    while (hi != 0) {
-      const int bit = __ffs(hi) - 1;
-      hi &= hi - 1;
-      sg = apply_table(&g_jump.v[fsa::kChunkLog2 + 10 + bit][0][0], sg);
-    }
-    const uint32_t off = (g * 32u + static_cast<uint32_t>(lane)) * kChunk;
-    if (off < nd) {
-      const uint64_t st = lane != 0 ? apply_table(&g_lanes1.v[lane][0][0], sg) : sg;
-      chunk_draws(st, take + off, nd - off < kChunk ? nd - off : kChunk, take,
-                  a.win2 + r * k2);
-    }
-    // A few fill blocks between draw groups.
-    for (int f = 0; f < kFillPerGroup && fill_left; ++f) {
-      unsigned long long item = 0;
-      if (lane == 0) item = atomicAdd(a.next, 1ULL);
-      item = __shfl_sync(0xffffffffU, item, 0);
-      if (static_cast<long long>(item) >= nfill) {
-        fill_left = false;
-      } else {
-        fill_block(a.fill, a.fill_vec4, static_cast<long long>(item), lane);
-      }
-    }
+    return;
   }
-  // Whatever fill is left once the draws are done.
-  while (fill_left) {
-    unsigned long long item = 0;
-    if (lane == 0) item = atomicAdd(a.next, 1ULL);
-    item = __shfl_sync(0xffffffffU, item, 0);
-    if (static_cast<long long>(item) >= nfill) break;
-    fill_block(a.fill, a.fill_vec4, static_cast<long long>(item), lane);
+  const long long ngroups = (total + 31) / 32;
+  const long long stride = static_cast<long long>(gridDim.x) * (warps - fillers);
+  for (long long G = static_cast<long long>(blockIdx.x) * (warps - fillers) + (warp - fillers);
+       G < ngroups; G += stride) {
+    const long long c = G * 32 + lane;
+    if (c < total) draw_chunk(a, rpre, s_k1, c);
+  }
+  if (nfill > 0) {
+    for (long long item = claim(a.next, lane); item < nfill; item = claim(a.next, lane)) {
+      fill_block(a.fill, a.fill_vec4, item, lane);
+    }
   }
 }
 
@@ -1074,8 +1084,13 @@ int draw_grid(int* grid_out) {
   int sms = 0, per_sm = 0;
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (err == cudaSuccess) {
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fsa_2hop_draw_kernel,
-                                                        kThreadsDraw, 8 * (kSmemRoots + 1));
+    const int smem = kDrawTableBytes + 8 * (kSmemRoots + 1);
+    err = cudaFuncSetAttribute(fsa_2hop_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem);
+    if (err == cudaSuccess) {
+      err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fsa_2hop_draw_kernel,
+                                                          kThreadsDraw, smem);
+    }
   }
   if (err != cudaSuccess) return cuda_fail(err);
   const int grid = sms * (per_sm > 0 ? per_sm : 1);
@@ -1226,7 +1241,8 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
   if (st != FSA_OK) return st;
   const Draw2Args da{rpre, lpre, state, mtake, mdraws, batch_size, fanout1, fanout2, win2,
                      next, fill4, fill_vec4, kSmemRoots};
-  const int dsmem = batch_size < kSmemRoots ? static_cast<int>(8 * (batch_size + 1)) : 0;
+  const int dsmem = kDrawTableBytes +
+                    (batch_size < kSmemRoots ? static_cast<int>(8 * (batch_size + 1)) : 0);
   st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st != FSA_OK) return st;
   const Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,

@@ -151,6 +151,24 @@ constexpr LaneTables make_lane_tables(int step_log2) {
   return t;
 }
 
+// The same tables with the lane index innermost: v[p][nib][l].  Threads
+// that apply different lane tables to different states read entry
+// [p][nib][l] -- in shared memory that is a different bank pair for every l
+// of a half-warp, whatever the nibbles.
+struct LaneTablesT {
+  uint64_t v[16][16][kLaneTables];
+};
+
+constexpr LaneTablesT transpose_lane_tables(const LaneTables& t) {
+  LaneTablesT o{};
+  for (int l = 0; l < kLaneTables; ++l) {
+    for (int p = 0; p < 16; ++p) {
+      for (int nib = 0; nib < 16; ++nib) o.v[p][nib][l] = t.v[l][p][nib];
+    }
+  }
+  return o;
+}
+
 // Host-side evaluation of T^n s (tests and host tools).
 inline uint64_t jump_host(const JumpTables& t, uint64_t s, uint64_t n) {
   for (int j = 0; j < kJumpBits && n != 0; ++j, n >>= 1) {

@@ -9,6 +9,21 @@
 static const fsa::JumpTables kTables = fsa::make_jump_tables();
 static const fsa::LaneTables kLanes1 = fsa::make_lane_tables(fsa::kChunkLog2);
 static const fsa::LaneTables kLanes2 = fsa::make_lane_tables(fsa::kChunkLog2 + 5);
+static const fsa::LaneTablesT kLanes1T = fsa::transpose_lane_tables(kLanes1);
+
+// Start state of chunk j as the 2-hop draw kernel forms it: the transposed
+// one-chunk table (entry [p][nib][j % 32]), then the 32-chunk table and the
+// jump matrices.
+static uint64_t chunk_start_transposed(uint64_t s0, uint64_t j) {
+  uint64_t s = 0;
+  for (int p = 0; p < 16; ++p) s ^= kLanes1T.v[p][(s0 >> (4 * p)) & 15][j % fsa::kLaneTables];
+  s = fsa::apply_nibbles(kLanes2.v[(j / fsa::kLaneTables) % fsa::kLaneTables], s);
+  uint64_t hi = j / (fsa::kLaneTables * fsa::kLaneTables);
+  for (int b = 0; hi != 0; ++b, hi >>= 1) {
+    if (hi & 1) s = fsa::apply_nibbles(kTables.v[fsa::kChunkLog2 + 10 + b], s);
+  }
+  return s;
+}
 
 int main() {
   char op[16];
@@ -20,6 +35,8 @@ int main() {
       // start state of chunk b of a row with initial state a
       std::printf("%llu\n", static_cast<unsigned long long>(
                                  fsa::chunk_start_host(kTables, kLanes1, kLanes2, a, b)));
+    } else if (std::strcmp(op, "chunkt") == 0) {
+      std::printf("%llu\n", static_cast<unsigned long long>(chunk_start_transposed(a, b)));
     } else if (std::strcmp(op, "stepmul") == 0) {
       // b steps with the multiply form of the xorshift step
       uint32_t lo = static_cast<uint32_t>(a), hi = static_cast<uint32_t>(a >> 32);

@@ -87,6 +87,8 @@ def test_chunk_start_equals_serial_steps(run):
     got = run([f"chunk {s} {j}" for s, j in cases])
     want = [str(oracle.xorshift_advance(s, j * chunk)) for s, j in cases]
     assert got == want
+    # the 2-hop draw kernel's form (one-chunk tables with the lane innermost)
+    assert run([f"chunkt {s} {j}" for s, j in cases]) == want
 
 
 def test_multiply_form_of_xorshift_step(run):
