@@ -13,11 +13,12 @@
 //     (atomicMax).  The slot then holds col[winner], or col[slot] if never
 //     replaced -- exactly what the serial loop leaves behind.
 //   * 2-hop forward = four launches: plan (CTA per root: first hop, table of
-//     second-hop rows), scan (one CTA: chunk prefix over all second-hop
-//     rows), draws (persistent grid; warps take 32 chunks at a time from a
-//     global counter, so hub rows and light rows balance across the GPU) and
-//     gather (one warp per (root, first-hop slot), no CTA barriers; the last
-//     warp of a root sums the slot means).
+//     second-hop rows), scan (one CTA: chunk prefix over the roots), draws
+//     (persistent grid; the chunks of all rows are numbered consecutively
+//     and a warp draws 32 consecutive chunks at a time, one per lane, so hub
+//     rows and light rows balance across the GPU; optionally the same kernel
+//     zeroes the backward's dense gradient with spare memory bandwidth) and
+//     gather (CTA per root: winners to ids, then the two-level mean).
 //   * Gather order = the reference's: per feature, leaves in j order from
 //     0.0f, / valid; slot means in i order, / non-empty (IEEE division), so
 //     forward outputs are bit-identical.  Rows are read with
@@ -543,13 +544,19 @@ struct Draw2Args {
   int smem_roots;                    // rpre staged in shared memory when B < this
 };
 
-// Fill work item: kFillItemVec4 float4 stores per lane (32 KB per warp).
-// The first kFillWarps warps of every CTA zero the buffer while the other
-// warps draw.
+// Fill work item: 32 KB (kFillItemVec4 float4 stores per lane of a warp).
+// Two fillers per CTA share the items: one thread driving the bulk-copy
+// (TMA) engine from a zeroed shared block, and one warp of streaming
+// stores.  Measured on the 2-hop power-law workload, this pair overlapped
+// the draws better than more store warps, than the bulk-copy engine alone,
+// or than draw warps that joined the fill after their draws.
 constexpr int kFillItemVec4 = 64;
-constexpr int kFillWarps = 4;
+constexpr int kFillWarps = 2;
+constexpr int kZeroBytes = 16384;   // zeroed shared source of the bulk copies
+constexpr int kFillInFlight = 8;    // bulk-copy groups in flight
 constexpr int kSmemRoots = 2048;
 constexpr int kDrawTableBytes = static_cast<int>(sizeof(fsa::LaneTablesT));  // 64 KB
+constexpr int kRprePad = (8 * (kSmemRoots + 1) + 15) & ~15;  // staged root prefix
 
 // Zeroes fill block `idx` (32 KB) with streaming stores.  A full block is
 // 64 stores per lane at immediate offsets from one address: the draws share
@@ -565,6 +572,34 @@ __device__ __forceinline__ void fill_block(float4* fill, int64_t fill_vec4, long
   } else {
     for (long long v = v0 + lane; v < fill_vec4; v += 32) __stcs(fill + v, z);
   }
+}
+
+// Zeroes fill items claimed from *counter until none is left, by bulk copies
+// (evict-first in L2) from the zeroed shared block at shared-window address
+// `zero`.  One thread; returns after its copies have completed.
+__device__ __forceinline__ void fill_items_bulk(unsigned long long* counter, float4* fill,
+                                                int64_t fill_vec4, uint32_t zero) {
+  constexpr int64_t kItem = 32LL * kFillItemVec4;
+  constexpr int64_t kPiece = kZeroBytes / 16;
+  const long long nitems = (fill_vec4 + kItem - 1) / kItem;
+  uint64_t policy = 0;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  bool issued = false;
+  for (long long item = static_cast<long long>(atomicAdd(counter, 1ULL)); item < nitems;
+       item = static_cast<long long>(atomicAdd(counter, 1ULL))) {
+    const int64_t v0 = item * kItem;
+    const int64_t v1 = fill_vec4 - v0 < kItem ? fill_vec4 : v0 + kItem;
+    for (int64_t v = v0; v < v1; v += kPiece) {
+      const uint32_t bytes = static_cast<uint32_t>((v1 - v < kPiece ? v1 - v : kPiece) * 16);
+      asm volatile(
+          "cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;"
+          :: "l"(fill + v), "r"(zero), "r"(bytes), "l"(policy) : "memory");
+    }
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(kFillInFlight) : "memory");
+    issued = true;
+  }
+  if (issued) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // Claims the next work item of counter `c` for the warp (lane 0 adds, the
@@ -635,16 +670,17 @@ __device__ __forceinline__ void draw_chunk(const Draw2Args& a, const long long* 
 // mostly share.
 //
 // Optionally the kernel also zeroes a buffer (the backward's dense
-// gradient) in 32 KB blocks claimed from the counter next[0], which the
-// plan kernel resets.  The draw loop is bound by integer issue, the fill by
-// HBM writes, so they run side by side in different warps: the first
-// kFillWarps warps of each CTA fill, the other warps draw and then help
-// with what is left of the fill.  (Warps that alternated between the two
-// would tie each one's progress to the other's.)
+// gradient) in 32 KB items claimed from the counter *next, which the plan
+// kernel resets.  The draw loop is bound by integer issue, the fill by HBM
+// writes, so they run side by side: warp 0 of each CTA drives the bulk-copy
+// engine (lane 0), warp 1 stores, the other warps draw.  (Warps that
+// alternated between the two would tie each one's progress to the
+// other's.)
 __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Draw2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint64_t* s_k1 = reinterpret_cast<uint64_t*>(smem_raw);  // one-chunk lane tables, [p][nib][l]
   long long* s_rpre = reinterpret_cast<long long*>(smem_raw + kDrawTableBytes);  // [B + 1]
+  float4* s_zero = reinterpret_cast<float4*>(smem_raw + kDrawTableBytes + kRprePad);
   const int lane = threadIdx.x & 31;
   const int64_t B = a.batch_size;
   const bool staged = B < a.smem_roots;
@@ -656,16 +692,29 @@ __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Dr
   if (staged) {
     for (int64_t t = threadIdx.x; t <= B; t += blockDim.x) s_rpre[t] = __ldg(a.rpre + t);
   }
+  if (a.fill_vec4 > 0) {
+    for (int t = threadIdx.x; t < kZeroBytes / 16; t += blockDim.x) {
+      s_zero[t] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+    }
+    // The zeros are read by the bulk-copy (async) proxy.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   __syncthreads();
   const long long* rpre = staged ? s_rpre : a.rpre;
   const long long total = rpre[B];
   const long long nfill = (a.fill_vec4 + 32LL * kFillItemVec4 - 1) / (32LL * kFillItemVec4);
-  // With a fill, the first kFillWarps warps of every CTA zero the buffer
-  // and the others draw; without one, every warp draws.  Groups of 32
-  // chunks cost about the same, so drawing warps take them round robin.
+  // Groups of 32 chunks cost about the same, so drawing warps take them
+  // round robin.
   const int warps = static_cast<int>(blockDim.x >> 5);
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const int fillers = nfill > 0 ? kFillWarps : 0;
+  if (warp == 0 && fillers > 0) {
+    if (lane == 0) {
+      fill_items_bulk(a.next, a.fill, a.fill_vec4,
+                      static_cast<uint32_t>(__cvta_generic_to_shared(s_zero)));
+    }
+    return;
+  }
   if (warp < fillers) {
     for (long long item = claim(a.next, lane); item < nfill; item = claim(a.next, lane)) {
       fill_block(a.fill, a.fill_vec4, item, lane);
@@ -678,11 +727,6 @@ __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Dr
        G < ngroups; G += stride) {
     const long long c = G * 32 + lane;
     if (c < total) draw_chunk(a, rpre, s_k1, c);
-  }
-  if (nfill > 0) {
-    for (long long item = claim(a.next, lane); item < nfill; item = claim(a.next, lane)) {
-      fill_block(a.fill, a.fill_vec4, item, lane);
-    }
   }
 }
 
@@ -1084,7 +1128,7 @@ int draw_grid(int* grid_out) {
   int sms = 0, per_sm = 0;
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (err == cudaSuccess) {
-    const int smem = kDrawTableBytes + 8 * (kSmemRoots + 1);
+    const int smem = kDrawTableBytes + kRprePad + kZeroBytes;
     err = cudaFuncSetAttribute(fsa_2hop_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem);
     if (err == cudaSuccess) {
@@ -1241,8 +1285,7 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
   if (st != FSA_OK) return st;
   const Draw2Args da{rpre, lpre, state, mtake, mdraws, batch_size, fanout1, fanout2, win2,
                      next, fill4, fill_vec4, kSmemRoots};
-  const int dsmem = kDrawTableBytes +
-                    (batch_size < kSmemRoots ? static_cast<int>(8 * (batch_size + 1)) : 0);
+  const int dsmem = kDrawTableBytes + kRprePad + (fill_vec4 > 0 ? kZeroBytes : 0);
   st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st != FSA_OK) return st;
   const Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
