@@ -54,9 +54,20 @@ PEAKS_PATH = REPO / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 NOMINAL_HBM_GBS = 8000.0
 
-# DRAM traffic per launch measured by ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum) for each kernel of a workload; see profiles/.
-NCU_TRAFFIC = {}
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum, in
+# bytes) that ncu measured for each kernel of a workload, from the captures
+# summarised in profiles/ (commands there).  The draw kernel with the fused
+# fill writes 918 MB of the 980 MB fill during its own launch; the rest
+# leaves L2 as dirty lines during the next kernels.
+NCU_TRAFFIC = {
+    "c2_2hop_powerlaw": {
+        "draw": 1.03e6 + 918.0e6,
+        "gather": 55.6e6 + 0.02e6,
+        "plan": 1.87e6,
+        "scan": 0.02e6,
+        "bwd": 42.5e6 + 2.2e6,
+    },
+}
 
 
 def log(*a):
@@ -209,14 +220,23 @@ class Inputs:
 
 
 def byte_model(w, inp: Inputs, batches: list[int]) -> dict:
-    """Algorithmic bytes per batch, averaged over `batches`, from the samples
-    the op itself draws (independent of the implementation)."""
+    """Algorithmic bytes per batch, per kernel, averaged over `batches`, from
+    the samples the op itself draws (independent of the implementation).
+
+    plan   = 4B (frontier) + 8(B + valid middles) (rowptr pairs) + 4 take1
+             (first-hop col ids) + 4 B k1 (saved first-hop ids)
+    draw   = 24 B k1 (second-hop row table: state, take, draws, prefix)
+             + 4 N D (the fused dense-gradient zero fill)
+    gather = 4 valid leaves (col ids) + 4 D valid leaves (feature rows)
+             + 4 D B (out) + 4 B k1 k2 (saved second-hop ids)
+    bwd    = 4 D B (grad_out) + saved ids + 8 D valid leaves (atomic RMW)
+    """
     import fusesampleagg_b200 as fsa
 
     k1, k2 = w.fanouts
     B, D = inp.B, w.dim
-    tot = {"fwd": 0.0, "bwd": 0.0, "unique_leaf_rows": 0.0, "valid_leaves": 0.0,
-           "rng_draws": 0.0}
+    keys = ("plan", "draw", "gather", "bwd", "unique_leaf_rows", "valid_leaves", "rng_draws")
+    tot = {k: 0.0 for k in keys}
     deg = (inp.rowptr[1:] - inp.rowptr[:-1]).long()
     with torch.no_grad():
         for i in batches:
@@ -225,23 +245,22 @@ def byte_model(w, inp: Inputs, batches: list[int]) -> dict:
                 replay_seed=inp.seeds[i], batch_offset=inp.offset)
             valid_mid = int((s1 >= 0).sum())
             valid_leaves = int((s2 >= 0).sum())
-            take1 = valid_mid
-            saved = 4 * (B * k1 + B * k1 * k2)
-            fwd = (4 * B + 8 * (B + valid_mid) + 4 * (take1 + valid_leaves)
-                   + 4 * D * valid_leaves + 4 * D * B + saved)
-            bwd = 4 * D * B + saved + 8 * D * valid_leaves
+            saved1, saved2 = 4 * B * k1, 4 * B * k1 * k2
+            tot["plan"] += 4 * B + 8 * (B + valid_mid) + 4 * valid_mid + saved1
+            tot["draw"] += 24 * B * k1 + 4.0 * inp.n * D
+            tot["gather"] += 4 * valid_leaves + 4 * D * valid_leaves + 4 * D * B + saved2
+            tot["bwd"] += 4 * D * B + saved1 + saved2 + 8 * D * valid_leaves
             # Reservoir draws (one xorshift64* output each) past the first
             # `fanout` positions of every sampled row: the sampler's work.
             mids = s1[s1 >= 0].long()
             tot["rng_draws"] += float((deg[inp.frontiers[i].long()] - k1).clamp_min(0).sum()
                                       + (deg[mids] - k2).clamp_min(0).sum())
             leaves = s2[s2 >= 0]
-            tot["fwd"] += fwd
-            tot["bwd"] += bwd
             tot["valid_leaves"] += valid_leaves
             tot["unique_leaf_rows"] += int(torch.unique(leaves).numel())
     n = max(len(batches), 1)
     out = {k: v / n for k, v in tot.items()}
+    out["scan"] = 16.0 * B  # root counts in, prefix out
     out["fill"] = 4.0 * inp.n * D
     return out
 
@@ -273,34 +292,68 @@ def make_step(api, w, inp: Inputs, batch_offset: bool):
 
 
 def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
-    """Public-API step with host buffers: pinned H2D of the roots and the
-    upstream gradient, D2H of the output into pinned memory."""
+    """Public-API step with host buffers: every step copies its roots and
+    upstream gradient from pinned host memory and reads its output back into
+    pinned memory.  As a data loader would, the copies run on a second
+    stream: step i's inputs are copied while step i-1 computes (double
+    buffered), and step i's output is read back while step i+1 computes.
+    `reset()` drops the prefetched inputs, so the first step after it copies
+    its own inputs before computing."""
     k1, k2 = w.fanouts
     nb = len(inp.frontiers)
     kw = {"batch_offset": inp.offset} if batch_offset else {}
+    dev = inp.x.device
     host_fr = [f.cpu().pin_memory() for f in inp.frontiers]
     host_go = inp.grad_out.cpu().pin_memory()
-    host_out = torch.empty((w.batch, w.dim), dtype=torch.float32).pin_memory()
-    dev = inp.x.device
+    host_out = [torch.empty((w.batch, w.dim), dtype=torch.float32).pin_memory() for _ in range(2)]
+    dev_fr = [torch.empty_like(inp.frontiers[0]) for _ in range(2)]
+    dev_go = [torch.empty_like(inp.grad_out) for _ in range(2)]
+    copy = torch.cuda.Stream(device=dev)
+    free = [None, None]       # event after the last compute that read a slot
+    prefetched = {}           # step -> event of its input copies
     h2d = host_fr[0].numel() * 4 + host_go.numel() * 4
-    d2h = host_out.numel() * 4
+    d2h = host_out[0].numel() * 4
+
+    def copy_inputs(i):
+        slot = i % 2
+        with torch.cuda.stream(copy):
+            if free[slot] is not None:
+                copy.wait_event(free[slot])
+            dev_fr[slot].copy_(host_fr[i % nb], non_blocking=True)
+            dev_go[slot].copy_(host_go, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy)
+        return ev
 
     def step(i):
-        j = i % nb
+        comp = torch.cuda.current_stream()
+        slot = i % 2
+        ready = prefetched.pop(i, None) or copy_inputs(i)
+        comp.wait_event(ready)
+        prefetched[i + 1] = copy_inputs(i + 1)
         inp.x.grad = None
-        fr = host_fr[j].to(dev, non_blocking=True)
-        go = host_go.to(dev, non_blocking=True)
-        out = api.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, fr, k1, k2,
-                                        replay_seed=inp.seeds[j], **kw)
-        out.backward(go)
-        host_out.copy_(out.detach(), non_blocking=True)
+        out = api.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, dev_fr[slot], k1, k2,
+                                        replay_seed=inp.seeds[i % nb], **kw)
+        out.backward(dev_go[slot])
+        done = torch.cuda.Event()
+        done.record(comp)
+        free[slot] = done
+        with torch.cuda.stream(copy):
+            copy.wait_event(done)
+            host_out[slot].copy_(out.detach(), non_blocking=True)
+        out.record_stream(copy)
 
+    step.reset = prefetched.clear
+    # the last output read-back belongs to the timed region
+    step.drain = lambda: torch.cuda.current_stream().wait_stream(copy)
     return step, h2d, d2h
 
 
 def timed(step, steps: int, warmup: int, dist: Dist, sampler=None, phase_events=False):
     for i in range(warmup):
         step(i)
+    if hasattr(step, "reset"):
+        step.reset()
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
@@ -316,6 +369,8 @@ def timed(step, steps: int, warmup: int, dist: Dist, sampler=None, phase_events=
             step(warmup + i, evs[i])
         else:
             step(warmup + i)
+    if hasattr(step, "drain"):
+        step.drain()
     end.record()
     torch.cuda.synchronize()
     t_wall1 = time.time()
@@ -333,8 +388,12 @@ def timed(step, steps: int, warmup: int, dist: Dist, sampler=None, phase_events=
 
 
 def kernel_times(w, inp: Inputs, iters: int) -> dict:
-    """Per-kernel CUDA-event durations through the C ABI on the current
-    stream (same inputs as the timed steps)."""
+    """Per-kernel CUDA-event durations (us) through the C ABI on the current
+    stream, same inputs as the timed steps.  The step's own configuration
+    first: the 2-hop forward with the dense-gradient zero fill fused into its
+    draw kernel, timed per kernel with the library's phase events, then the
+    backward.  For comparison: the forward without the fill and the
+    stand-alone fill kernel."""
     from fusesampleagg_b200 import _lib
 
     L = _lib.LIB
@@ -348,29 +407,52 @@ def kernel_times(w, inp: Inputs, iters: int) -> dict:
     ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, k1, k2, 1, 1)
     ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
-    names = ("fill", "fwd", "bwd")
-    acc = {k: 0.0 for k in names}
     x = inp.x.detach()
-    for it in range(iters + 3):
-        j = it % len(inp.frontiers)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        ev[0].record()
-        _lib.check(L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fill")
-        ev[1].record()
+
+    def fwd(j, fill):
         _lib.check(L.fsa_sample_agg_2hop_forward(
             inp.rowptr.data_ptr(), inp.col.data_ptr(), n, inp.col.numel(), x.data_ptr(), D,
             inp.frontiers[j].data_ptr(), B, inp.offset, k1, k2, inp.seeds[j], out.data_ptr(),
-            s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, None, 0, stream), "fwd")
-        ev[2].record()
+            s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes,
+            grad.data_ptr() if fill else None, grad.numel() if fill else 0, stream), "fwd")
+
+    def bwd():
         _lib.check(L.fsa_sample_agg_2hop_backward(
             inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
             grad.data_ptr(), n, stream), "bwd")
-        ev[3].record()
+
+    nb = len(inp.frontiers)
+    for it in range(3):
+        fwd(it % nb, True)
+        bwd()
+    torch.cuda.synchronize()
+    res = {"bwd": 0.0, "fwd_nofill": 0.0, "fill_alone": 0.0}
+    _lib.phase_timing(True)
+    try:
+        for it in range(iters):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            fwd(it % nb, True)
+            ev[0].record()
+            bwd()
+            ev[1].record()
+            torch.cuda.synchronize()
+            res["bwd"] += ev[0].elapsed_time(ev[1])
+        phases, calls = _lib.phase_times()
+    finally:
+        _lib.phase_timing(False)
+    for it in range(iters):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        _lib.check(L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fill")
+        ev[1].record()
+        fwd(it % nb, False)
+        ev[2].record()
         torch.cuda.synchronize()
-        if it >= 3:
-            for k, name in enumerate(names):
-                acc[name] += ev[k].elapsed_time(ev[k + 1])
-    return {k: v / iters for k, v in acc.items()}
+        res["fill_alone"] += ev[0].elapsed_time(ev[1])
+        res["fwd_nofill"] += ev[1].elapsed_time(ev[2])
+    times = {k: 1000.0 * v / calls for k, v in phases.items()}
+    times.update({k: 1000.0 * v / iters for k, v in res.items()})
+    return times
 
 
 # ---------------------------------------------------------------------------
@@ -454,12 +536,16 @@ def run(args) -> None:
         sampler.start()
     launches0 = api.launch_count() if args.impl == "ours" else None
     step = make_step(api, w, inp, batch_offset=args.impl == "ours")
-    ms, phases = timed(step, args.steps, args.warmup, dist, sampler, phase_events=True)
+    ms, _ = timed(step, args.steps, args.warmup, dist, sampler)
     launches = (api.launch_count() - launches0) if args.impl == "ours" else None
     clocks = sampler.stop() if sampler else None
     # Launches counted above include the warm-up steps: report the timed ones.
     if launches is not None:
         launches = launches * args.steps // (args.steps + args.warmup)
+
+    # forward / backward split from a shorter pass with events between them
+    # (kept out of the timed region above)
+    _, phases = timed(step, min(args.steps, 100), args.warmup, dist, phase_events=True)
 
     e2e_step, h2d, d2h = make_e2e_step(api, w, inp, batch_offset=args.impl == "ours")
     e2e_ms, _ = timed(e2e_step, args.steps, args.warmup, dist)
@@ -501,26 +587,39 @@ def run(args) -> None:
         },
         "phases_ms": phases,
         "e2e": {"value": e2e_value, "unit": "roots/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                "d2h_bytes_per_step": d2h,
+                "copies": "roots + upstream gradient H2D from pinned memory one step ahead "
+                          "on a copy stream (double-buffered), output D2H into pinned memory "
+                          "overlapping the next step; first step copies its own inputs"},
         "clocks": clocks,
     }
     if args.impl == "ours":
         kt = kernel_times(w, inp, iters=min(args.steps, 30))
+        names = {
+            "plan": "fsa_2hop_plan_kernel (first hop, second-hop row table)",
+            "scan": "fsa_2hop_scan_kernel (chunk prefix over roots)",
+            "draw": "fsa_2hop_draw_kernel (second-hop reservoir draws + fused dense-grad "
+                    "zero fill)",
+            "gather": "fsa_2hop_gather_kernel (winners to ids, two-level mean)",
+            "bwd": "fsa_2hop_backward_kernel (replay scatter, red.global.add.v4)",
+            "fill": "fsa_fill_zero_kernel (stand-alone zero fill, not in the step)",
+        }
         kernels = {}
-        for name in ("fill", "fwd", "bwd"):
-            t = kt[name] / 1000.0
-            achieved = bytes_model[name] / t / 1e9
+        for name in ("plan", "scan", "draw", "gather", "bwd", "fill"):
+            us = kt["fill_alone"] if name == "fill" else kt[name]
+            achieved = bytes_model[name] / (us * 1e-6) / 1e9
             kernels[name] = {
-                "avg_us": kt[name] * 1000.0,
+                "kernel": names[name],
+                "avg_us": us,
                 "algorithmic_bytes": int(bytes_model[name]),
                 "achieved_gbs": achieved,
                 "frac_of_measured_hbm": achieved / peak,
                 "frac_of_8tbs": achieved / NOMINAL_HBM_GBS,
             }
-        kernels["fwd"]["kernel"] = "fsa_2hop_forward_kernel (sample + gather)"
-        kernels["bwd"]["kernel"] = "fsa_2hop_backward_kernel (replay scatter, red.global.add.v4)"
-        kernels["fill"]["kernel"] = "fsa_fill_zero_kernel (dense grad zero-fill)"
-        dom = max(("fill", "fwd", "bwd"), key=lambda k: kt[k])
+        kernels["draw"]["rng_draws_per_launch"] = bytes_model["rng_draws"]
+        kernels["draw"]["rng_draws_per_s"] = bytes_model["rng_draws"] / (kt["draw"] * 1e-6)
+        kernels["forward_without_fill_us"] = kt["fwd_nofill"]
+        dom = max(("plan", "scan", "draw", "gather", "bwd"), key=lambda k: kt[k])
         traffic = NCU_TRAFFIC.get(args.workload, {}).get(dom)
         result["roofline"] = {
             "kernel": kernels[dom]["kernel"],
@@ -550,6 +649,46 @@ def run(args) -> None:
         print(json.dumps(result))
 
 
+def profile_forward(args) -> None:
+    """A fixed, short sequence of C-ABI calls on one GPU for ncu captures:
+    `--calls` 2-hop forwards of the workload (different root batches), each
+    followed by its backward; `--profile-forward fused` zeroes the gradient
+    inside the forward (the step's configuration), `separate` with the
+    stand-alone fill kernel, `none` runs forwards only."""
+    from fusesampleagg_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = synthetic.WORKLOADS[args.workload]
+    inp = Inputs(w, dev, 0, 1, args.calls)
+    L = _lib.LIB
+    k1, k2 = w.fanouts
+    B, D, n = inp.B, w.dim, inp.n
+    out = torch.empty((B, D), device=dev)
+    s1 = torch.empty((B, k1), dtype=torch.int32, device=dev)
+    s2 = torch.empty((B, k1, k2), dtype=torch.int32, device=dev)
+    grad = torch.empty((n, D), device=dev) if args.profile_forward != "none" else None
+    ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, k1, k2, 1, 1)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    fused = args.profile_forward == "fused"
+    for j in range(args.calls):
+        if args.profile_forward == "separate":
+            _lib.check(L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fill")
+        _lib.check(L.fsa_sample_agg_2hop_forward(
+            inp.rowptr.data_ptr(), inp.col.data_ptr(), n, inp.col.numel(), inp.x.data_ptr(), D,
+            inp.frontiers[j].data_ptr(), B, 0, k1, k2, inp.seeds[j], out.data_ptr(),
+            s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes,
+            grad.data_ptr() if fused else None, grad.numel() if fused else 0, stream), "fwd")
+        if grad is not None:
+            _lib.check(L.fsa_sample_agg_2hop_backward(
+                inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
+                grad.data_ptr(), n, stream), "bwd")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_forward": args.profile_forward, "calls": args.calls,
+                      "workload": args.workload}))
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -561,7 +700,13 @@ def main() -> None:
     p.add_argument("--batches", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-budget", type=float, default=12.0)
+    p.add_argument("--profile-forward", choices=["fused", "separate", "none"],
+                   help="run a short C-ABI call sequence for ncu instead of the benchmark")
+    p.add_argument("--calls", type=int, default=3, help="calls of --profile-forward")
     args = p.parse_args()
+    if args.profile_forward:
+        profile_forward(args)
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     ws = int(os.environ.get("WORLD_SIZE", "1"))

@@ -46,6 +46,8 @@ SIGNATURES = {
     "fsa_sample_agg_2hop_backward": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),
+    "fsa_phase_timing": (_int, [_int]),
+    "fsa_phase_times": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
     "fsa_status_string": (ctypes.c_char_p, [_int]),
     "fsa_last_cuda_error": (_int, []),
     "fsa_launch_count": (_u64, []),
@@ -82,6 +84,21 @@ def check(status: int, what: str) -> None:
         code = LIB.fsa_last_cuda_error()
         raise RuntimeError(f"{what} failed: {text} (cudaError {code})")
     raise RuntimeError(f"{what} failed: {text}")
+
+
+def phase_timing(enable: bool) -> None:
+    """Starts (clearing old records) or stops per-kernel event timing of
+    the 2-hop forward."""
+    check(LIB.fsa_phase_timing(int(bool(enable))), "fsa_phase_timing")
+
+
+def phase_times() -> tuple[dict, int]:
+    """Summed milliseconds of the recorded 2-hop forwards' plan, scan, draw
+    and gather kernels, and the number of recorded calls."""
+    ms = (ctypes.c_double * 4)()
+    calls = _i64(0)
+    check(LIB.fsa_phase_times(ms, ctypes.byref(calls)), "fsa_phase_times")
+    return dict(zip(("plan", "scan", "draw", "gather"), list(ms))), int(calls.value)
 
 
 def launch_count() -> int:

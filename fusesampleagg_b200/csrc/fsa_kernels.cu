@@ -29,9 +29,12 @@
 //     and reported in a per-device status word.
 #include <cuda_runtime.h>
 
+#include <array>
 #include <atomic>
 #include <climits>
 #include <cstdint>
+#include <mutex>
+#include <vector>
 
 #include "fsa_rng.cuh"
 #include "fsa_sm100.h"
@@ -1062,6 +1065,36 @@ int launch(Kernel kernel, int grid, int block, int smem, cudaStream_t stream,
 
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
+// Optional per-kernel timing of the 2-hop forward (fsa_phase_timing): five
+// events per call, around plan, scan, draw and gather.  Off by default; the
+// forward then records nothing.
+constexpr int kPhases = 4;
+std::atomic<bool> g_timing{false};
+std::mutex g_timing_mu;
+std::vector<std::array<cudaEvent_t, kPhases + 1>> g_timing_calls;
+
+struct PhaseEvents {
+  std::array<cudaEvent_t, kPhases + 1> ev{};
+  bool on = false;
+  int mark(int k, cudaStream_t s) {
+    if (!on) return FSA_OK;
+    const cudaError_t err = cudaEventRecord(ev[k], s);
+    return err == cudaSuccess ? FSA_OK : cuda_fail(err);
+  }
+};
+
+int phase_events_begin(PhaseEvents* pe) {
+  pe->on = g_timing.load(std::memory_order_relaxed);
+  if (!pe->on) return FSA_OK;
+  for (auto& e : pe->ev) {
+    const cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) return cuda_fail(err);
+  }
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  g_timing_calls.push_back(pe->ev);
+  return FSA_OK;
+}
+
 // Workspace of the 2-hop forward, in bytes from a 256-byte aligned base.
 struct Ws2 {
   size_t rpre, rgroups, lpre, state, mbeg, mtake, mdraws, next, s1, win2, total;
@@ -1274,11 +1307,17 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
   const Plan2Args pa{rowptr, col, num_nodes, num_edges, frontier, batch_size, batch_offset,
                      fanout1, fanout2, seed, s1, win2, mbeg, mtake, mdraws, state, lpre,
                      rgroups, next};
+  PhaseEvents pe;
+  int st = phase_events_begin(&pe);
+  if (st == FSA_OK) st = pe.mark(0, s);
+  if (st != FSA_OK) return st;
   const int psmem = ((4 * fanout1 + 15) & ~15) + 8 * fanout1;
-  int st = launch(fsa_2hop_plan_kernel, grid_for(batch_size), kThreadsPlan, psmem, s, pa);
+  st = launch(fsa_2hop_plan_kernel, grid_for(batch_size), kThreadsPlan, psmem, s, pa);
+  if (st == FSA_OK) st = pe.mark(1, s);
   if (st != FSA_OK) return st;
   const Scan2Args sa{rgroups, rpre, batch_size};
   st = launch(fsa_2hop_scan_kernel, 1, kThreadsScan, 0, s, sa);
+  if (st == FSA_OK) st = pe.mark(2, s);
   if (st != FSA_OK) return st;
   int dgrid = 0;
   st = draw_grid(&dgrid);
@@ -1287,15 +1326,18 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
                      next, fill4, fill_vec4, kSmemRoots};
   const int dsmem = kDrawTableBytes + kRprePad + (fill_vec4 > 0 ? kZeroBytes : 0);
   st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
+  if (st == FSA_OK) st = pe.mark(3, s);
   if (st != FSA_OK) return st;
   const Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
                        mtake, win2, samples2, out, dchunk};
   const int ggrid = grid_for(batch_size);
   switch (vec) {
-    case 4: return launch(fsa_2hop_gather_kernel<4>, ggrid, kThreadsGather, gsmem, s, ga);
-    case 2: return launch(fsa_2hop_gather_kernel<2>, ggrid, kThreadsGather, gsmem, s, ga);
-    default: return launch(fsa_2hop_gather_kernel<1>, ggrid, kThreadsGather, gsmem, s, ga);
+    case 4: st = launch(fsa_2hop_gather_kernel<4>, ggrid, kThreadsGather, gsmem, s, ga); break;
+    case 2: st = launch(fsa_2hop_gather_kernel<2>, ggrid, kThreadsGather, gsmem, s, ga); break;
+    default: st = launch(fsa_2hop_gather_kernel<1>, ggrid, kThreadsGather, gsmem, s, ga); break;
   }
+  if (st == FSA_OK) st = pe.mark(4, s);
+  return st;
 }
 
 int fsa_sample_agg_2hop_backward(const float* grad_out, const int32_t* samples1,
@@ -1349,6 +1391,38 @@ int fsa_fill_zero_f32(float* dst, int64_t count, void* stream) {
     fsa_fill_zero_scalar_kernel<<<sms * 8, kThreadsFill, 0, s>>>(dst, count);
   }
   return check_launch();
+}
+
+int fsa_phase_timing(int enable) {
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  if (enable) {
+    for (auto& call : g_timing_calls) {
+      for (auto e : call) cudaEventDestroy(e);
+    }
+    g_timing_calls.clear();
+  }
+  g_timing.store(enable != 0, std::memory_order_relaxed);
+  return FSA_OK;
+}
+
+int fsa_phase_times(double* ms, int64_t* calls) {
+  if (ms == nullptr || calls == nullptr) return FSA_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  for (int k = 0; k < kPhases; ++k) ms[k] = 0.0;
+  int status = FSA_OK;
+  for (auto& call : g_timing_calls) {
+    for (int k = 0; k < kPhases && status == FSA_OK; ++k) {
+      float t = 0.0F;
+      cudaError_t err = cudaEventSynchronize(call[k + 1]);
+      if (err == cudaSuccess) err = cudaEventElapsedTime(&t, call[k], call[k + 1]);
+      if (err != cudaSuccess) status = cuda_fail(err);
+      ms[k] += t;
+    }
+    for (auto e : call) cudaEventDestroy(e);
+  }
+  *calls = static_cast<int64_t>(g_timing_calls.size());
+  g_timing_calls.clear();
+  return status;
 }
 
 const char* fsa_status_string(int status) {

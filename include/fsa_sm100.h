@@ -181,6 +181,19 @@ FSA_API int fsa_sample_agg_2hop_backward(const float* grad_out, const int32_t* s
  */
 FSA_API int fsa_fill_zero_f32(float* dst, int64_t count, void* stream);
 
+/*
+ * Per-kernel timing of fsa_sample_agg_2hop_forward, for benchmarks (no
+ * counterpart in the reference).  fsa_phase_timing(1) discards earlier
+ * records and makes every later 2-hop forward record CUDA events around its
+ * plan, scan, draw and gather kernels on the call's stream;
+ * fsa_phase_timing(0) stops recording.  fsa_phase_times waits for the
+ * recorded events, writes the summed milliseconds of the four kernels to
+ * ms[0..3] and the number of recorded calls to *calls, and releases the
+ * records.  Off by default: the forward then creates and records nothing.
+ */
+FSA_API int fsa_phase_timing(int enable);
+FSA_API int fsa_phase_times(double* ms, int64_t* calls);
+
 /* Human-readable text for a status code (static storage). */
 FSA_API const char* fsa_status_string(int status);
 

@@ -134,3 +134,11 @@ def test_check_raises_runtime_error():
     with pytest.raises(RuntimeError, match="invalid argument"):
         _lib.check(_lib.FSA_ERR_INVALID_ARGUMENT, "x")
     _lib.check(_lib.FSA_OK, "x")
+
+
+def test_phase_timing_without_calls_needs_no_cuda():
+    _lib.phase_timing(True)
+    times, calls = _lib.phase_times()
+    _lib.phase_timing(False)
+    assert calls == 0 and all(v == 0.0 for v in times.values())
+    assert L.fsa_phase_times(None, None) == _lib.FSA_ERR_INVALID_ARGUMENT

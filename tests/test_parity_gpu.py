@@ -183,6 +183,24 @@ def test_empty_frontier():
     assert fsa.fused_sample_agg_2hop(rp, cl, x, fr, 3, 2).shape == (0, 16)
 
 
+def test_phase_timing_records_each_forward_kernel():
+    from fusesampleagg_b200 import _lib
+
+    _lib.phase_timing(True)
+    try:
+        out, s1, s2, ref_out, r1, r2 = run_2hop("powerlaw", 15, 10, 3, batch=64)
+        run_2hop("powerlaw", 15, 10, 4, batch=64)
+        times, calls = _lib.phase_times()
+    finally:
+        _lib.phase_timing(False)
+    assert calls == 2
+    assert all(v > 0.0 for v in times.values()), times
+    np.testing.assert_array_equal(s2.cpu().numpy(), r2)
+    # recording stopped: later forwards add nothing
+    run_2hop("powerlaw", 15, 10, 5, batch=64)
+    assert _lib.phase_times()[1] == 0
+
+
 @pytest.mark.parametrize("name,fan", [("toy", (3, 2)), ("powerlaw", (15, 10)), ("hub", (5, 10)),
                                       ("powerlaw", (8, 4))])
 def test_2hop_backward_matches_oracle(name, fan):
