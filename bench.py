@@ -508,14 +508,14 @@ def load_reference_op():
 
 
 def run(args) -> None:
+    # Both arms run on every rank: the reference is a GPU op, so at N GPUs it
+    # gets N GPUs too (each rank times its own slice of roots; the reference
+    # API has no batch offset, so its ranks draw their own ids).
     dist = Dist()
-    if args.impl == "reference" and dist.rank != 0:
-        return
     torch.cuda.set_device(dist.local_rank)
     dev = torch.device("cuda", dist.local_rank)
-    world = dist.world if args.impl == "ours" else 1
-    if args.impl == "ours":
-        dist.init()
+    world = dist.world
+    dist.init()
     w = synthetic.WORKLOADS[args.workload]
     if w.hops != 2:
         raise SystemExit("bench.py times the 2-hop workloads")
@@ -524,9 +524,11 @@ def run(args) -> None:
     else:
         api = load_reference_op()
         if api is None:
-            print(json.dumps({"impl": "reference",
-                              "unavailable": "reference op not built into oracle/_ref "
-                                             "(python -m oracle.build --ref)"}))
+            if dist.rank == 0:
+                print(json.dumps({"impl": "reference",
+                                  "unavailable": "reference op not built into oracle/_ref "
+                                                 "(python -m oracle.build --ref)"}))
+            dist.close()
             return
     batches = args.batches
     inp = Inputs(w, dev, dist.rank, world, batches)
