@@ -12,8 +12,9 @@
 //     records, per reservoir slot, the largest position that selected it
 //     (atomicMax).  The slot then holds col[winner], or col[slot] if never
 //     replaced -- exactly what the serial loop leaves behind.
-//   * 2-hop forward = four launches: plan (CTA per root: first hop, table of
-//     second-hop rows), scan (one CTA: chunk prefix over the roots), draws
+//   * 2-hop forward = three launches (four from 2048 roots up): plan (CTA
+//     per root: first hop, table of second-hop rows), [scan (one CTA: chunk
+//     prefix over the roots; smaller batches scan it in each draw CTA)], draws
 //     (persistent grid; the chunks of all rows are numbered consecutively
 //     and a warp draws 32 consecutive chunks at a time, one per lane, so hub
 //     rows and light rows balance across the GPU; optionally the same kernel
@@ -478,26 +479,29 @@ struct Scan2Args {
 
 constexpr int kScanItems = 4;
 
-// One CTA, tiles of blockDim * kScanItems entries: each thread scans its
-// contiguous items, warp shuffles and the warp totals give the tile prefix,
-// a running carry joins the tiles.
-__global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2Args a) {
-  __shared__ long long warp_sums[kThreadsScan / 32];
-  __shared__ long long carry;
+// Exclusive prefix of counts[0, n) into pre[0, n], pre[n] = total, by one
+// CTA of at most 1024 threads: tiles of blockDim * kScanItems entries; each
+// thread scans its contiguous items, warp shuffles and the warp totals give
+// the tile prefix, a running carry joins the tiles.  `warp_sums` ([32]) and
+// `carry` are shared scratch; pre may be global or shared memory.  All
+// threads of the CTA must call it.
+__device__ __forceinline__ void block_exclusive_scan(const long long* counts, long long* pre,
+                                                     int64_t n, long long* warp_sums,
+                                                     long long* carry) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int nw = blockDim.x >> 5;
-  if (tid == 0) carry = 0;
+  if (tid == 0) *carry = 0;
   __syncthreads();
   const int64_t tile = static_cast<int64_t>(blockDim.x) * kScanItems;
-  for (int64_t t0 = 0; t0 < a.n; t0 += tile) {
+  for (int64_t t0 = 0; t0 < n; t0 += tile) {
     const int64_t i0 = t0 + static_cast<int64_t>(tid) * kScanItems;
     long long v[kScanItems];
     long long local = 0;
 #pragma unroll
     for (int u = 0; u < kScanItems; ++u) {
-      v[u] = i0 + u < a.n ? a.counts[i0 + u] : 0;
+      v[u] = i0 + u < n ? counts[i0 + u] : 0;
       local += v[u];
     }
     long long incl = local;
@@ -518,21 +522,32 @@ __global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2
       if (lane < nw) warp_sums[lane] = w;
     }
     __syncthreads();
-    long long run = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - local;
+    long long run = *carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - local;
 #pragma unroll
     for (int u = 0; u < kScanItems; ++u) {
-      if (i0 + u < a.n) a.pre[i0 + u] = run;
+      if (i0 + u < n) pre[i0 + u] = run;
       run += v[u];
     }
     __syncthreads();
-    if (tid == 0) carry += warp_sums[nw - 1];
+    if (tid == 0) *carry += warp_sums[nw - 1];
     __syncthreads();
   }
-  if (tid == 0) a.pre[a.n] = carry;
+  if (tid == 0) pre[n] = *carry;
+  __syncthreads();
+}
+
+// Chunk prefix over the roots when it does not fit the draw kernel's shared
+// memory (batches of kSmemRoots roots or more; smaller batches are scanned
+// by every draw CTA itself).
+__global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2Args a) {
+  __shared__ long long warp_sums[32];
+  __shared__ long long carry;
+  block_exclusive_scan(a.counts, a.pre, a.n, warp_sums, &carry);
 }
 
 struct Draw2Args {
-  const long long* rpre;             // [B + 1] chunk prefix over roots
+  const long long* rgroups;          // [B] chunks per root
+  const long long* rpre;             // [B + 1] chunk prefix over roots (B >= smem_roots)
   const long long* lpre;             // [R] chunk prefix of each row within its root
   const unsigned long long* state;   // [R]
   const int32_t* mtake;              // [R]
@@ -693,7 +708,9 @@ __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Dr
     for (int t = threadIdx.x; t < kDrawTableBytes / 16; t += blockDim.x) dst[t] = __ldg(src + t);
   }
   if (staged) {
-    for (int64_t t = threadIdx.x; t <= B; t += blockDim.x) s_rpre[t] = __ldg(a.rpre + t);
+    // the chunk prefix over the roots, scanned by this CTA (no scan kernel)
+    __shared__ long long s_scan[33];
+    block_exclusive_scan(a.rgroups, s_rpre, B, s_scan, s_scan + 32);
   }
   if (a.fill_vec4 > 0) {
     for (int t = threadIdx.x; t < kZeroBytes / 16; t += blockDim.x) {
@@ -1315,15 +1332,18 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
   st = launch(fsa_2hop_plan_kernel, grid_for(batch_size), kThreadsPlan, psmem, s, pa);
   if (st == FSA_OK) st = pe.mark(1, s);
   if (st != FSA_OK) return st;
-  const Scan2Args sa{rgroups, rpre, batch_size};
-  st = launch(fsa_2hop_scan_kernel, 1, kThreadsScan, 0, s, sa);
+  // Batches below kSmemRoots roots are scanned inside the draw kernel.
+  if (batch_size >= kSmemRoots) {
+    const Scan2Args sa{rgroups, rpre, batch_size};
+    st = launch(fsa_2hop_scan_kernel, 1, kThreadsScan, 0, s, sa);
+  }
   if (st == FSA_OK) st = pe.mark(2, s);
   if (st != FSA_OK) return st;
   int dgrid = 0;
   st = draw_grid(&dgrid);
   if (st != FSA_OK) return st;
-  const Draw2Args da{rpre, lpre, state, mtake, mdraws, batch_size, fanout1, fanout2, win2,
-                     next, fill4, fill_vec4, kSmemRoots};
+  const Draw2Args da{rgroups, rpre, lpre, state, mtake, mdraws, batch_size, fanout1, fanout2,
+                     win2, next, fill4, fill_vec4, kSmemRoots};
   const int dsmem = kDrawTableBytes + kRprePad + (fill_vec4 > 0 ? kZeroBytes : 0);
   st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st == FSA_OK) st = pe.mark(3, s);

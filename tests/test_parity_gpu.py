@@ -82,6 +82,23 @@ def run_2hop(name, k1, k2, seed, dim=33, batch=64, root_seed=0, offset=0):
     return out, s1, s2, ref_out, r1, r2
 
 
+def test_large_batch_uses_scan_kernel_and_matches_oracle():
+    """2048+ roots: the root prefix no longer fits the draw kernel's shared
+    memory and a separate scan kernel runs (plan, scan, draws, gather)."""
+    g = cpu_graph("uniform")
+    rp, cl = dev_graph("uniform")
+    x = cpu_features(g.num_nodes, 8)
+    fr = C.frontier_for("uniform", g, 3000, 9)
+    before = fsa.launch_count()
+    out, s1, s2 = fsa.fused_sample_agg_2hop_with_samples(rp, cl, x.cuda(), fr.cuda(), 5, 4,
+                                                         replay_seed=21)
+    assert fsa.launch_count() == before + 4
+    r1, r2 = oracle.sample_2hop(g.rowptr.numpy(), g.col.numpy(), fr.numpy(), 5, 4, 21)
+    np.testing.assert_array_equal(s1.cpu().numpy(), r1)
+    np.testing.assert_array_equal(s2.cpu().numpy(), r2)
+    assert_bit_equal(out, oracle.forward_2hop(x.numpy(), r2))
+
+
 # ---------------------------------------------------------------------------
 # 1-hop
 # ---------------------------------------------------------------------------
@@ -285,8 +302,8 @@ def test_launch_count_advances():
     x = cpu_features(8, 12).cuda()
     before = fsa.launch_count()
     fsa.fused_sample_agg_2hop(rp, cl, x, frontier("toy").cuda(), 3, 2)
-    # plan, scan, draws, gather
-    assert fsa.launch_count() == before + 4
+    # plan, draws (the root prefix is scanned in the draw kernel), gather
+    assert fsa.launch_count() == before + 3
     before = fsa.launch_count()
     fsa.fused_sample_agg(rp, cl, x, frontier("toy").cuda(), 3)
     assert fsa.launch_count() == before + 1
