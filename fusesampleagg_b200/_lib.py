@@ -22,6 +22,8 @@ FSA_STATUS_BAD_NEIGHBOR = 0x4
 
 MAX_FANOUT_1HOP = 1024
 MAX_2HOP_ENTRIES = 12000
+MAX_SHARDS = 64
+IPC_HANDLE_BYTES = 64
 NOALLOC_SCRATCH_BYTES = 4194304
 
 # Every symbol include/fsa_sm100.h declares, with (restype, argtypes).
@@ -43,11 +45,20 @@ SIGNATURES = {
     "fsa_sample_agg_2hop_forward_noalloc": (
         _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p,
                _p, _i64, _p]),
+    "fsa_sample_agg_2hop_forward_sharded": (
+        _int, [_p, _p, _i64, _i64, ctypes.POINTER(_p), _i64, _i32, _i64, _p, _i64, _i64, _i32,
+               _i32, _u64, _p, _p, _p, _p, ctypes.c_size_t, _p, _i64, _p]),
+    "fsa_sample_agg_2hop_backward_sharded": (
+        _int, [_p, _p, _p, _i64, _i64, _i32, _i32, ctypes.POINTER(_p), _i64, _i32, _i64, _p]),
     "fsa_sample_agg_2hop_backward": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),
     "fsa_phase_timing": (_int, [_int]),
     "fsa_phase_times": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
+    "fsa_ipc_export": (_int, [_p, _p, ctypes.POINTER(_u64)]),
+    "fsa_ipc_open": (_int, [_p, _int, ctypes.POINTER(_p)]),
+    "fsa_ipc_close": (_int, [_p, _int]),
+    "fsa_enable_peer_access": (_int, [_int, _int]),
     "fsa_status_string": (ctypes.c_char_p, [_int]),
     "fsa_last_cuda_error": (_int, []),
     "fsa_launch_count": (_u64, []),

@@ -34,6 +34,7 @@
 #include <atomic>
 #include <climits>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -750,6 +751,22 @@ __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Dr
   }
 }
 
+// Feature (or gradient) rows block-partitioned over up to FSA_MAX_SHARDS
+// devices: global row r lives in shard r / rows at local row r % rows.  The
+// bases are device pointers valid in this process -- the local shard and
+// peers' shards mapped over NVLink (CUDA IPC).  Passed by value.
+struct RowShards {
+  float* base[FSA_MAX_SHARDS];
+  int64_t rows;
+  int n;
+};
+
+// Row `id` (0 <= id < n * rows) of a table with row stride d.
+__device__ __forceinline__ float* shard_row(const RowShards& t, int32_t id, int64_t d) {
+  const uint32_t s = static_cast<uint32_t>(id) / static_cast<uint32_t>(t.rows);
+  return t.base[s] + (static_cast<int64_t>(id) - static_cast<int64_t>(s) * t.rows) * d;
+}
+
 struct Gather2Args {
   const int32_t* col;
   const float* x;
@@ -764,6 +781,7 @@ struct Gather2Args {
   int32_t* samples2;     // optional id output; may alias win2
   float* out;
   int dchunk;            // feature tile width (multiple of the vector width)
+  RowShards xs;          // sharded feature rows (kSharded kernels only)
 };
 
 // Shared-memory layout of the gather kernel, in bytes.
@@ -790,7 +808,7 @@ constexpr int kGatherBatch = 8;
 // that kGatherBatch rows are in flight per thread) and divides by the valid
 // count; then the slot means are summed in slot order and divided by the
 // non-empty count (fused_sample_agg.cu:189-213).
-template <int V>
+template <int V, bool kSharded>
 __global__ void __launch_bounds__(kThreadsGather)
     fsa_2hop_gather_kernel(const Gather2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -841,7 +859,10 @@ __global__ void __launch_bounds__(kThreadsGather)
           for (int u = 0; u < kGatherBatch; ++u) {
             const int32_t leaf = j0 + u < k2 ? leaves[j0 + u] : -1;
             ok[u] = leaf >= 0 && leaf < N;
-            if (ok[u]) rows[u] = load_stream<V>(base + static_cast<int64_t>(leaf) * D);
+            if (ok[u]) {
+              rows[u] = load_stream<V>(kSharded ? shard_row(a.xs, leaf, D) + f0 + v * V
+                                                : base + static_cast<int64_t>(leaf) * D);
+            }
             if (leaf >= N && v == 0 && f0 == 0) flag_status(FSA_STATUS_BAD_NEIGHBOR);
           }
 #pragma unroll
@@ -935,6 +956,7 @@ __global__ void __launch_bounds__(kThreadsBwd)
 }
 
 struct Bwd2Args {
+  RowShards gs;          // sharded gradient rows (kSharded kernels only)
   const float* grad_out;
   const int32_t* samples1;
   const int32_t* samples2;
@@ -947,7 +969,7 @@ struct Bwd2Args {
 };
 
 // One CTA per root; items are (first-hop slot, feature vector) pairs.
-template <int V>
+template <int V, bool kSharded>
 __global__ void __launch_bounds__(kThreadsBwd)
     fsa_2hop_backward_kernel(const Bwd2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -992,7 +1014,9 @@ __global__ void __launch_bounds__(kThreadsBwd)
           const int32_t leaf = leaves[j];
           if (leaf < 0) continue;
           if (leaf < a.num_nodes) {
-            red_add<V>(a.grad_x + static_cast<int64_t>(leaf) * a.feature_dim + v * V, g);
+            red_add<V>(kSharded ? shard_row(a.gs, leaf, a.feature_dim) + v * V
+                                : a.grad_x + static_cast<int64_t>(leaf) * a.feature_dim + v * V,
+                       g);
           } else if (v == 0) {
             flag_status(FSA_STATUS_BAD_NEIGHBOR);
           }
@@ -1260,16 +1284,15 @@ size_t fsa_sample_agg_2hop_workspace_size(int64_t batch_size, int32_t fanout1,
   return ws2_layout(batch_size, fanout1, fanout2, has_samples1 == 0, has_samples2 == 0).total;
 }
 
-int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
-                                int64_t num_nodes, int64_t num_edges,
-                                const float* x, int64_t feature_dim,
-                                const int32_t* frontier, int64_t batch_size,
-                                int64_t batch_offset, int32_t fanout1,
-                                int32_t fanout2, uint64_t seed, float* out,
-                                int32_t* samples1, int32_t* samples2,
-                                void* workspace, size_t workspace_bytes,
-                                float* zero_fill, int64_t zero_count,
-                                void* stream) {
+// The 2-hop forward; `xs` (optional) reads the feature rows from a shard
+// table instead of x.
+static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_nodes,
+                        int64_t num_edges, const float* x, int64_t feature_dim,
+                        const int32_t* frontier, int64_t batch_size, int64_t batch_offset,
+                        int32_t fanout1, int32_t fanout2, uint64_t seed, float* out,
+                        int32_t* samples1, int32_t* samples2, void* workspace,
+                        size_t workspace_bytes, float* zero_fill, int64_t zero_count,
+                        void* stream, const RowShards* xs) {
   if (fanout1 < 0 || fanout2 < 0 || batch_size < 0 || feature_dim < 0 ||
       num_nodes < 0 || num_edges < 0 || batch_offset < 0 || zero_count < 0 ||
       (zero_count > 0 && zero_fill == nullptr)) {
@@ -1348,23 +1371,87 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
   st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st == FSA_OK) st = pe.mark(3, s);
   if (st != FSA_OK) return st;
-  const Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
-                       mtake, win2, samples2, out, dchunk};
+  Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
+                 mtake, win2, samples2, out, dchunk, RowShards{}};
   const int ggrid = grid_for(batch_size);
-  switch (vec) {
-    case 4: st = launch(fsa_2hop_gather_kernel<4>, ggrid, kThreadsGather, gsmem, s, ga); break;
-    case 2: st = launch(fsa_2hop_gather_kernel<2>, ggrid, kThreadsGather, gsmem, s, ga); break;
-    default: st = launch(fsa_2hop_gather_kernel<1>, ggrid, kThreadsGather, gsmem, s, ga); break;
+  if (xs != nullptr) {
+    ga.xs = *xs;
+    switch (vec) {
+      case 4: st = launch(fsa_2hop_gather_kernel<4, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
+      case 2: st = launch(fsa_2hop_gather_kernel<2, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
+      default: st = launch(fsa_2hop_gather_kernel<1, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
+    }
+  } else {
+    switch (vec) {
+      case 4: st = launch(fsa_2hop_gather_kernel<4, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
+      case 2: st = launch(fsa_2hop_gather_kernel<2, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
+      default: st = launch(fsa_2hop_gather_kernel<1, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
+    }
   }
   if (st == FSA_OK) st = pe.mark(4, s);
   return st;
 }
 
-int fsa_sample_agg_2hop_backward(const float* grad_out, const int32_t* samples1,
-                                 const int32_t* samples2, int64_t batch_size,
-                                 int64_t feature_dim, int32_t fanout1,
-                                 int32_t fanout2, float* grad_x,
-                                 int64_t num_nodes, void* stream) {
+int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
+                                int64_t num_nodes, int64_t num_edges,
+                                const float* x, int64_t feature_dim,
+                                const int32_t* frontier, int64_t batch_size,
+                                int64_t batch_offset, int32_t fanout1,
+                                int32_t fanout2, uint64_t seed, float* out,
+                                int32_t* samples1, int32_t* samples2,
+                                void* workspace, size_t workspace_bytes,
+                                float* zero_fill, int64_t zero_count,
+                                void* stream) {
+  return forward_2hop(rowptr, col, num_nodes, num_edges, x, feature_dim, frontier, batch_size,
+                      batch_offset, fanout1, fanout2, seed, out, samples1, samples2, workspace,
+                      workspace_bytes, zero_fill, zero_count, stream, nullptr);
+}
+
+// Shard table from a host array of device pointers; checks the count, the
+// partition covers num_nodes, every base is non-null and aligned to 16
+// bytes when the rows are float4 vectors (else to the vector width).
+static int make_shards(float* const* bases, int64_t shard_rows, int32_t num_shards,
+                       int64_t num_nodes, int64_t feature_dim, RowShards* t) {
+  if (bases == nullptr || num_shards < 1 || num_shards > FSA_MAX_SHARDS || shard_rows < 1 ||
+      shard_rows > 0x7fffffffLL || num_nodes > shard_rows * num_shards) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  *t = RowShards{};
+  t->rows = shard_rows;
+  t->n = num_shards;
+  const int vec = feature_dim % 4 == 0 ? 4 : (feature_dim % 2 == 0 ? 2 : 1);
+  for (int k = 0; k < num_shards; ++k) {
+    if (bases[k] == nullptr || !aligned(bases[k], 4 * vec)) return FSA_ERR_INVALID_ARGUMENT;
+    t->base[k] = bases[k];
+  }
+  return FSA_OK;
+}
+
+int fsa_sample_agg_2hop_forward_sharded(const int32_t* rowptr, const int32_t* col,
+                                        int64_t num_nodes, int64_t num_edges,
+                                        const float* const* x_shards, int64_t shard_rows,
+                                        int32_t num_shards, int64_t feature_dim,
+                                        const int32_t* frontier, int64_t batch_size,
+                                        int64_t batch_offset, int32_t fanout1,
+                                        int32_t fanout2, uint64_t seed, float* out,
+                                        int32_t* samples1, int32_t* samples2,
+                                        void* workspace, size_t workspace_bytes,
+                                        float* zero_fill, int64_t zero_count,
+                                        void* stream) {
+  RowShards t;
+  if (num_nodes < 0 || feature_dim < 0) return FSA_ERR_INVALID_ARGUMENT;
+  const int st = make_shards(const_cast<float* const*>(x_shards), shard_rows, num_shards,
+                             num_nodes, feature_dim, &t);
+  if (st != FSA_OK) return st;
+  return forward_2hop(rowptr, col, num_nodes, num_edges, t.base[0], feature_dim, frontier,
+                      batch_size, batch_offset, fanout1, fanout2, seed, out, samples1, samples2,
+                      workspace, workspace_bytes, zero_fill, zero_count, stream, &t);
+}
+
+static int backward_2hop(const float* grad_out, const int32_t* samples1,
+                         const int32_t* samples2, int64_t batch_size, int64_t feature_dim,
+                         int32_t fanout1, int32_t fanout2, float* grad_x, int64_t num_nodes,
+                         void* stream, const RowShards* gs) {
   if (fanout1 < 0 || fanout2 < 0 || batch_size < 0 || feature_dim < 0 ||
       num_nodes < 0) {
     return FSA_ERR_INVALID_ARGUMENT;
@@ -1378,17 +1465,48 @@ int fsa_sample_agg_2hop_backward(const float* grad_out, const int32_t* samples1,
       (num_nodes > 0 && grad_x == nullptr)) {
     return FSA_ERR_INVALID_ARGUMENT;
   }
-  Bwd2Args a{grad_out, samples1, samples2, batch_size, feature_dim,
+  Bwd2Args a{RowShards{}, grad_out, samples1, samples2, batch_size, feature_dim,
              fanout1, fanout2, grad_x, num_nodes};
   const int vec = pick_vec(feature_dim, grad_out, grad_x);
   const int smem = 4 * (fanout1 + fanout1 * fanout2 + 1);
   const int grid = grid_for(batch_size);
   auto s = static_cast<cudaStream_t>(stream);
-  switch (vec) {
-    case 4: return launch(fsa_2hop_backward_kernel<4>, grid, kThreadsBwd, smem, s, a);
-    case 2: return launch(fsa_2hop_backward_kernel<2>, grid, kThreadsBwd, smem, s, a);
-    default: return launch(fsa_2hop_backward_kernel<1>, grid, kThreadsBwd, smem, s, a);
+  if (gs != nullptr) {
+    a.gs = *gs;
+    switch (vec) {
+      case 4: return launch(fsa_2hop_backward_kernel<4, true>, grid, kThreadsBwd, smem, s, a);
+      case 2: return launch(fsa_2hop_backward_kernel<2, true>, grid, kThreadsBwd, smem, s, a);
+      default: return launch(fsa_2hop_backward_kernel<1, true>, grid, kThreadsBwd, smem, s, a);
+    }
   }
+  switch (vec) {
+    case 4: return launch(fsa_2hop_backward_kernel<4, false>, grid, kThreadsBwd, smem, s, a);
+    case 2: return launch(fsa_2hop_backward_kernel<2, false>, grid, kThreadsBwd, smem, s, a);
+    default: return launch(fsa_2hop_backward_kernel<1, false>, grid, kThreadsBwd, smem, s, a);
+  }
+}
+
+int fsa_sample_agg_2hop_backward(const float* grad_out, const int32_t* samples1,
+                                 const int32_t* samples2, int64_t batch_size,
+                                 int64_t feature_dim, int32_t fanout1,
+                                 int32_t fanout2, float* grad_x,
+                                 int64_t num_nodes, void* stream) {
+  return backward_2hop(grad_out, samples1, samples2, batch_size, feature_dim, fanout1, fanout2,
+                       grad_x, num_nodes, stream, nullptr);
+}
+
+int fsa_sample_agg_2hop_backward_sharded(const float* grad_out, const int32_t* samples1,
+                                         const int32_t* samples2, int64_t batch_size,
+                                         int64_t feature_dim, int32_t fanout1,
+                                         int32_t fanout2, float* const* grad_shards,
+                                         int64_t shard_rows, int32_t num_shards,
+                                         int64_t num_nodes, void* stream) {
+  RowShards t;
+  if (num_nodes < 0 || feature_dim < 0) return FSA_ERR_INVALID_ARGUMENT;
+  const int st = make_shards(grad_shards, shard_rows, num_shards, num_nodes, feature_dim, &t);
+  if (st != FSA_OK) return st;
+  return backward_2hop(grad_out, samples1, samples2, batch_size, feature_dim, fanout1, fanout2,
+                       t.base[0], num_nodes, stream, &t);
 }
 
 int fsa_fill_zero_f32(float* dst, int64_t count, void* stream) {
@@ -1443,6 +1561,88 @@ int fsa_phase_times(double* ms, int64_t* calls) {
   *calls = static_cast<int64_t>(g_timing_calls.size());
   g_timing_calls.clear();
   return status;
+}
+
+int fsa_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return FSA_ERR_INVALID_ARGUMENT;
+  // Base of the allocation that holds ptr (an IPC handle names a whole
+  // allocation), through the driver's cuMemGetAddressRange.
+  using AddressRange = int (*)(unsigned long long*, size_t*, unsigned long long);
+  static AddressRange range = nullptr;
+  if (range == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    const cudaError_t err = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn,
+                                                    cudaEnableDefault, &q);
+    if (err != cudaSuccess) return cuda_fail(err);
+    if (q != cudaDriverEntryPointSuccess || fn == nullptr) return FSA_ERR_CUDA;
+    range = reinterpret_cast<AddressRange>(fn);
+  }
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<unsigned long long>(ptr)) != 0 || base == 0) {
+    return FSA_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess) return cuda_fail(err);
+  static_assert(sizeof(cudaIpcMemHandle_t) == FSA_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<unsigned long long>(ptr) - base;
+  return FSA_OK;
+}
+
+int fsa_ipc_open(const void* handle, int device, void** base) {
+  if (handle == nullptr || base == nullptr) return FSA_ERR_INVALID_ARGUMENT;
+  int prev = 0;
+  cudaError_t err = cudaGetDevice(&prev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  err = cudaSetDevice(device);
+  // Opened in the accessing device's context: the mapping belongs to that
+  // device's address space and peer access to the owner is enabled with it.
+  if (err == cudaSuccess) err = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  const cudaError_t err2 = cudaSetDevice(prev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (err2 != cudaSuccess) return cuda_fail(err2);
+  return FSA_OK;
+}
+
+int fsa_ipc_close(void* base, int device) {
+  if (base == nullptr) return FSA_ERR_INVALID_ARGUMENT;
+  int prev = 0;
+  cudaError_t err = cudaGetDevice(&prev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  err = cudaSetDevice(device);
+  if (err == cudaSuccess) err = cudaIpcCloseMemHandle(base);
+  const cudaError_t err2 = cudaSetDevice(prev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (err2 != cudaSuccess) return cuda_fail(err2);
+  return FSA_OK;
+}
+
+int fsa_enable_peer_access(int device, int peer) {
+  if (device == peer) return FSA_OK;
+  int prev = 0;
+  cudaError_t err = cudaGetDevice(&prev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  int can = 0;
+  err = cudaDeviceCanAccessPeer(&can, device, peer);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (!can) return FSA_ERR_INVALID_ARGUMENT;
+  err = cudaSetDevice(device);
+  if (err == cudaSuccess) {
+    err = cudaDeviceEnablePeerAccess(peer, 0);
+    if (err == cudaErrorPeerAccessAlreadyEnabled) {
+      cudaGetLastError();  // reset the last-error state this call set
+      err = cudaSuccess;
+    }
+  }
+  const cudaError_t err2 = cudaSetDevice(prev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (err2 != cudaSuccess) return cuda_fail(err2);
+  return FSA_OK;
 }
 
 const char* fsa_status_string(int status) {

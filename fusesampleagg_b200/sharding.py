@@ -42,3 +42,209 @@ def allreduce_gradient(grad: torch.Tensor, group=None) -> torch.Tensor:
 
     dist.all_reduce(grad, op=dist.ReduceOp.SUM, group=group)
     return grad
+
+
+# ---------------------------------------------------------------------------
+# Row-sharded features (one process per GPU, peers over NVLink)
+# ---------------------------------------------------------------------------
+
+def shard_span(num_nodes: int, rank: int, world: int) -> tuple[int, int]:
+    """Rows [start, stop) of a `num_nodes`-row table held by `rank`: blocks
+    of ceil(num_nodes / world) rows, the last block shorter."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    rows = -(-num_nodes // world) if num_nodes > 0 else 1
+    start = min(rank * rows, num_nodes)
+    return start, min(start + rows, num_nodes)
+
+
+class ShardedFeatures:
+    """A float32 feature table block-partitioned by row over the ranks of a
+    NCCL process group, one GPU per rank, plus its gradient shards.
+
+    Rank r holds rows ``shard_span(num_nodes, r, world)`` in `local` (a
+    contiguous [rows, D] tensor on its GPU) and their gradient in `grad`.
+    Construction is collective: every rank exports its two shards as CUDA
+    IPC handles and maps the others' into its own device's address space, so
+    the kernels read remote feature rows and add into remote gradient rows
+    directly over NVLink.  Call `close()` on every rank (collective) before
+    the process group is destroyed.
+    """
+
+    def __init__(self, local: torch.Tensor, num_nodes: int, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if not local.is_cuda or local.dtype != torch.float32 or local.dim() != 2:
+            raise ValueError("local shard must be a 2-D float32 CUDA tensor")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.num_nodes = int(num_nodes)
+        start, stop = shard_span(self.num_nodes, self.rank, self.world)
+        if local.size(0) != stop - start:
+            raise ValueError(f"rank {self.rank} must hold rows [{start}, {stop})")
+        if self.world > _lib.MAX_SHARDS:
+            raise ValueError(f"at most {_lib.MAX_SHARDS} shards")
+        self.start, self.stop = start, stop
+        self.shard_rows = -(-self.num_nodes // self.world) if self.num_nodes > 0 else 1
+        self.dim = int(local.size(1))
+        self.local = local.contiguous()
+        self.grad = torch.zeros_like(self.local)
+        self._flag = torch.zeros(1, device=self.local.device)
+        self._device = self.local.device.index
+        L = _lib.LIB
+
+        def export(t):
+            if t.numel() == 0:
+                return None
+            h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+            off = ctypes.c_uint64(0)
+            _lib.check(L.fsa_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "fsa_ipc_export")
+            return h.raw, off.value
+
+        shared = [None] * self.world
+        dist.all_gather_object(shared, (export(self.local), export(self.grad)), group=group)
+        # Map every peer allocation once, into this device's address space.
+        self._mapped = {}
+        xs, gs = [], []
+        for r, (xe, ge) in enumerate(shared):
+            if r == self.rank:
+                xs.append(self.local.data_ptr())
+                gs.append(self.grad.data_ptr())
+                continue
+            for e, out in ((xe, xs), (ge, gs)):
+                if e is None:  # an empty trailing shard: any aligned base
+                    out.append(self.local.data_ptr())
+                    continue
+                handle, off = e
+                if handle not in self._mapped:
+                    base = ctypes.c_void_p()
+                    _lib.check(L.fsa_ipc_open(handle, self._device, ctypes.byref(base)),
+                               "fsa_ipc_open")
+                    self._mapped[handle] = base.value
+                out.append(self._mapped[handle] + off)
+        ptrs = ctypes.c_void_p * self.world
+        self.x_ptrs = ptrs(*xs)
+        self.grad_ptrs = ptrs(*gs)
+
+    def device_barrier(self) -> None:
+        """Orders the GPUs: the current stream of every rank waits until every
+        rank's previously queued work has finished (an NCCL all-reduce of one
+        float on the current stream; no host synchronisation)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        """Unmaps the peers' shards (collective: call on every rank; no rank
+        frees its shards before every rank has unmapped them)."""
+        import torch.distributed as dist
+
+        from . import _lib
+
+        torch.cuda.synchronize(self.local.device)
+        dist.barrier(group=self.group)
+        for base in self._mapped.values():
+            _lib.check(_lib.LIB.fsa_ipc_close(base, self._device), "fsa_ipc_close")
+        self._mapped.clear()
+        self.x_ptrs = self.grad_ptrs = None
+        dist.barrier(group=self.group)
+
+
+def _forward_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier, fanout1, fanout2,
+                          seed, capture, batch_offset, zero):
+    from . import _as_int64, _as_seed, _check_fanout_2hop, _check_offset, _DeviceGuard
+    from . import _lib, _ptr, _stream_handle
+
+    L = _lib.LIB
+    for t, name in ((rowptr, "rowptr"), (col, "col"), (frontier, "frontier")):
+        if not t.is_cuda or t.dtype != torch.int32 or t.device != feats.local.device:
+            raise RuntimeError(f"{name} must be an int32 tensor on the shard's device")
+    if rowptr.numel() != feats.num_nodes + 1:
+        raise RuntimeError("rowptr size must be num_nodes + 1")
+    fanout1 = _as_int64(fanout1, "fanout1")
+    fanout2 = _as_int64(fanout2, "fanout2")
+    _check_fanout_2hop(fanout1, fanout2)
+    seed = _as_seed(seed)
+    off = _check_offset(batch_offset)
+    B, D, dev = frontier.size(0), feats.dim, feats.local.device
+    with _DeviceGuard(dev):
+        if B == 0 or fanout1 == 0 or fanout2 == 0:
+            out = torch.zeros((B, D), dtype=torch.float32, device=dev)
+            s1 = torch.full((B, fanout1), -1, dtype=torch.int32, device=dev)
+            s2 = torch.full((B, fanout1, fanout2), -1, dtype=torch.int32, device=dev)
+            if zero is not None:
+                zero.zero_()
+            return out, s1, s2
+        out = torch.empty((B, D), dtype=torch.float32, device=dev)
+        s1 = torch.empty((B, fanout1), dtype=torch.int32, device=dev) if capture else None
+        s2 = torch.empty((B, fanout1, fanout2), dtype=torch.int32, device=dev) if capture else None
+        ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, int(capture),
+                                                        int(capture))
+        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+        st = L.fsa_sample_agg_2hop_forward_sharded(
+            rowptr.data_ptr(), col.data_ptr(), feats.num_nodes, col.numel(), feats.x_ptrs,
+            feats.shard_rows, feats.world, D, frontier.data_ptr(), B, off, fanout1, fanout2,
+            seed, out.data_ptr(), _ptr(s1), _ptr(s2), ws.data_ptr(), ws_bytes, _ptr(zero),
+            zero.numel() if zero is not None else 0, _stream_handle(dev))
+        _lib.check(st, "fsa_sample_agg_2hop_forward_sharded")
+    return out, s1, s2
+
+
+class _Sharded2HopFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, local, rowptr, col, frontier, fanout1, fanout2, replay_seed, batch_offset,
+                feats):
+        capture = local.requires_grad
+        out, s1, s2 = _forward_2hop_sharded(rowptr.contiguous(), col.contiguous(), feats,
+                                            frontier.contiguous(), fanout1, fanout2,
+                                            replay_seed, capture, batch_offset,
+                                            feats.grad if capture else None)
+        if capture:
+            # every rank's gradient shard is zero before any rank's backward
+            # adds into it
+            feats.device_barrier()
+            ctx.save_for_backward(s1, s2)
+        ctx.feats = feats
+        ctx.capture = capture
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        from . import _DeviceGuard, _lib, _stream_handle
+
+        if ctx.capture:
+            feats = ctx.feats
+            s1, s2 = ctx.saved_tensors
+            g = grad_out.contiguous()
+            B, D = g.shape
+            with _DeviceGuard(g.device):
+                st = _lib.LIB.fsa_sample_agg_2hop_backward_sharded(
+                    g.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, s1.size(1), s2.size(2),
+                    feats.grad_ptrs, feats.shard_rows, feats.world, feats.num_nodes,
+                    _stream_handle(g.device))
+                _lib.check(st, "fsa_sample_agg_2hop_backward_sharded")
+            # every rank's additions into this rank's shard are complete
+            feats.device_barrier()
+        ctx.feats = None
+        return (None,) * 9
+
+
+def fused_sample_agg_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier, fanout1,
+                                  fanout2, replay_seed=1234, batch_offset=0):
+    """2-hop fused sample + mean aggregate over row-sharded features.
+
+    Same ids and outputs as ``fused_sample_agg_2hop`` on the whole table
+    (with the same `batch_offset`).  When ``feats.local.requires_grad`` the
+    forward zeroes ``feats.grad`` and the backward adds this rank's roots'
+    feature gradients into the owning ranks' ``feats.grad`` (over NVLink);
+    after the backward, ``feats.grad`` on every rank holds the gradient of its
+    rows summed over all ranks' roots.  Collective when training: every rank
+    must call forward and backward the same number of times.
+    """
+    return _Sharded2HopFn.apply(feats.local, rowptr, col, frontier, fanout1, fanout2,
+                                replay_seed, batch_offset, feats)

@@ -47,6 +47,8 @@ extern "C" {
 #define FSA_MAX_FANOUT_1HOP 1024
 #define FSA_MAX_2HOP_ENTRIES 12000 /* fanout1 + fanout1 * fanout2 */
 #define FSA_NOALLOC_SCRATCH_BYTES 4194304 /* scratch of the _noalloc entry point */
+#define FSA_MAX_SHARDS 64 /* feature / gradient row shards of the _sharded entry points */
+#define FSA_IPC_HANDLE_BYTES 64
 
 /* Bits of the per-device status word (fsa_device_status). */
 #define FSA_STATUS_BAD_ROOT 0x1u     /* frontier id outside [0, num_nodes) */
@@ -161,6 +163,72 @@ FSA_API int fsa_sample_agg_2hop_forward_noalloc(const int32_t* rowptr, const int
                                                 int32_t* samples1, int32_t* samples2,
                                                 float* zero_fill, int64_t zero_count,
                                                 void* stream);
+
+/*
+ * 2-hop forward and backward on row-sharded features: the multi-GPU mode
+ * for feature tables larger than one device's memory.  No
+ * counterpart in the reference, whose binding requires the whole table on
+ * one device (fuseop/binding.cpp:35).
+ *
+ * Feature row r (0 <= r < num_nodes) lives in shard r / shard_rows at local
+ * row r % shard_rows; x_shards / grad_shards are HOST arrays of num_shards
+ * (<= FSA_MAX_SHARDS) device pointers valid in the calling process -- the
+ * local shard and the other devices' shards mapped over NVLink (CUDA IPC).
+ * Each shard holds shard_rows rows of feature_dim floats (the last may be
+ * shorter as long as num_nodes <= shard_rows * num_shards); bases aligned
+ * to 16 bytes when feature_dim % 4 == 0 (8 when % 2 == 0).  The graph
+ * (rowptr, col) is whole on every device.  Everything else is as in
+ * fsa_sample_agg_2hop_forward / _backward: the same ids and outputs as the
+ * unsharded call on the concatenated table; the backward adds into the
+ * owning shard's gradient (atomics over NVLink for remote rows).
+ *
+ * Ordering across devices is the caller's: the shards must not change
+ * during the forward, and every gradient shard must be zeroed (e.g. by its
+ * own forward's zero_fill) before any device's backward starts.
+ */
+FSA_API int fsa_sample_agg_2hop_forward_sharded(const int32_t* rowptr, const int32_t* col,
+                                                int64_t num_nodes, int64_t num_edges,
+                                                const float* const* x_shards, int64_t shard_rows,
+                                                int32_t num_shards, int64_t feature_dim,
+                                                const int32_t* frontier, int64_t batch_size,
+                                                int64_t batch_offset, int32_t fanout1,
+                                                int32_t fanout2, uint64_t seed, float* out,
+                                                int32_t* samples1, int32_t* samples2,
+                                                void* workspace, size_t workspace_bytes,
+                                                float* zero_fill, int64_t zero_count,
+                                                void* stream);
+
+FSA_API int fsa_sample_agg_2hop_backward_sharded(const float* grad_out, const int32_t* samples1,
+                                                 const int32_t* samples2, int64_t batch_size,
+                                                 int64_t feature_dim, int32_t fanout1,
+                                                 int32_t fanout2, float* const* grad_shards,
+                                                 int64_t shard_rows, int32_t num_shards,
+                                                 int64_t num_nodes, void* stream);
+
+/*
+ * Sharing shards between processes (one process per GPU), no counterpart in
+ * the reference.  fsa_ipc_export writes the CUDA IPC handle
+ * (FSA_IPC_HANDLE_BYTES bytes) of the allocation holding `ptr` and ptr's
+ * byte offset in it.  fsa_ipc_open maps a handle from another process into
+ * `device`'s address space (the device whose kernels will access it; peer
+ * access to the owner is enabled with the mapping) and returns the
+ * allocation's base there: the shard is base + offset.  fsa_ipc_close
+ * unmaps it.  The exporting process must keep the allocation alive until
+ * every importer has closed it.
+ */
+FSA_API int fsa_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+FSA_API int fsa_ipc_open(const void* handle, int device, void** base);
+FSA_API int fsa_ipc_close(void* base, int device);
+
+/*
+ * Lets kernels on `device` read and write `peer`'s memory in this process
+ * (cudaDeviceEnablePeerAccess; already-enabled is not an error).  Needed
+ * before the _sharded entry points touch shards that live on other devices:
+ * a peer's shard mapped through CUDA IPC is addressable, but a kernel on
+ * another device may only access it once peer access is enabled.  Returns
+ * FSA_ERR_INVALID_ARGUMENT when the two devices cannot access each other.
+ */
+FSA_API int fsa_enable_peer_access(int device, int peer);
 
 /*
  * 2-hop backward (saved-index replay).  Replaces
