@@ -89,6 +89,10 @@ class Dist:
         if self.world > 1 and not self.pg:
             import torch.distributed as dist
 
+            # rank 0's stdout carries exactly one JSON line: keep NCCL's
+            # version banner off it unless the caller asked for NCCL logs
+            os.environ.setdefault("NCCL_DEBUG", "WARN")
+
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local_rank))
             self.pg = True
@@ -495,6 +499,35 @@ def cpu_baseline(w, inp: Inputs, budget_s: float = 12.0) -> dict:
 # Arms
 # ---------------------------------------------------------------------------
 
+def sharded_api(inp: Inputs, w):
+    """The package's API with the features row-sharded over the ranks: this
+    rank keeps only its rows, the others' are mapped over NVLink.  Returns an
+    object with the `fused_sample_agg_2hop` / `launch_count` calls the steps
+    use (its x argument is ignored) and the ShardedFeatures."""
+    import fusesampleagg_b200 as fsa
+    from fusesampleagg_b200 import sharding
+
+    start, stop = sharding.shard_span(inp.n, int(os.environ.get("RANK", "0")),
+                                      int(os.environ.get("WORLD_SIZE", "1")))
+    local = inp.x.detach()[start:stop].clone().requires_grad_(True)
+    feats = sharding.ShardedFeatures(local, inp.n)
+    # the whole table is not needed any more: keep a 1-row stand-in so that
+    # the steps' `x.grad = None` still works
+    inp.x = torch.zeros((1, w.dim), device=local.device, requires_grad=True)
+    torch.cuda.empty_cache()
+
+    class Api:
+        @staticmethod
+        def fused_sample_agg_2hop(rowptr, col, x, frontier, k1, k2, replay_seed=1234,
+                                  batch_offset=0):
+            return sharding.fused_sample_agg_2hop_sharded(rowptr, col, feats, frontier, k1, k2,
+                                                          replay_seed, batch_offset)
+
+        launch_count = staticmethod(fsa.launch_count)
+
+    return Api, feats
+
+
 def load_reference_op():
     ref_dir = REPO / "oracle" / "_ref" / "fuseop"
     if not (ref_dir / "__init__.py").exists():
@@ -533,6 +566,11 @@ def run(args) -> None:
     batches = args.batches
     inp = Inputs(w, dev, dist.rank, world, batches)
     log(f"[rank {dist.rank}] setup {inp.setup_s:.1f}s graph {inp.stats}")
+    feats = None
+    if args.sharded:
+        if args.impl != "ours" or world < 2:
+            raise SystemExit("--sharded times this package on 2+ GPUs (torchrun)")
+        api, feats = sharded_api(inp, w)
     sampler = ClockSampler(dist.local_rank) if dist.rank == 0 else None
     if sampler:
         sampler.start()
@@ -556,8 +594,10 @@ def run(args) -> None:
     value = units / (ms / 1000.0)
     e2e_value = units / (e2e_ms / 1000.0)
     used = sorted({(args.warmup + i) % batches for i in range(args.steps)})
-    bytes_model = byte_model(w, inp, used[: min(len(used), 16)])
+    bytes_model = byte_model(w, inp, used[: min(len(used), 16)]) if feats is None else None
     peak, peak_kind = load_peaks()
+    if feats is not None:
+        feats.close()
 
     result = {
         "metric": METRIC,
@@ -581,8 +621,13 @@ def run(args) -> None:
             "roots_per_gpu": w.batch,
             "global_batch": w.batch * world,
             "root_batches": batches,
-            "parallelism": f"roots partitioned over {world} GPU(s), graph and features "
-                           "replicated, no data-path collective",
+            "parallelism": (f"roots partitioned over {world} GPU(s), graph replicated, "
+                            "feature rows and their gradient block-sharded over the GPUs "
+                            "(remote rows read and gradient added over NVLink through peer "
+                            "pointers; one-float NCCL all-reduce after forward and backward "
+                            "as the cross-GPU ordering)" if feats is not None else
+                            f"roots partitioned over {world} GPU(s), graph and features "
+                            "replicated, no data-path collective"),
             "l2": "inputs larger than L2: x (%.0f MB) gathered at random and the dense "
                   "gradient (%.0f MB) rewritten every step" % (
                       inp.n * w.dim * 4 / 1e6, inp.n * w.dim * 4 / 1e6),
@@ -595,7 +640,10 @@ def run(args) -> None:
                           "overlapping the next step; first step copies its own inputs"},
         "clocks": clocks,
     }
-    if args.impl == "ours":
+    if feats is not None:
+        result["mode"] = "sharded"
+        result["gpu_launches"] = launches
+    elif args.impl == "ours":
         kt = kernel_times(w, inp, iters=min(args.steps, 30))
         names = {
             "plan": "fsa_2hop_plan_kernel (first hop, second-hop row table)",
@@ -702,6 +750,8 @@ def main() -> None:
     p.add_argument("--batches", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-budget", type=float, default=12.0)
+    p.add_argument("--sharded", action="store_true",
+                   help="row-shard the features over the ranks (peer reads over NVLink)")
     p.add_argument("--profile-forward", choices=["fused", "separate", "none"],
                    help="run a short C-ABI call sequence for ncu instead of the benchmark")
     p.add_argument("--calls", type=int, default=3, help="calls of --profile-forward")
