@@ -142,3 +142,26 @@ def test_phase_timing_without_calls_needs_no_cuda():
     _lib.phase_timing(False)
     assert calls == 0 and all(v == 0.0 for v in times.values())
     assert L.fsa_phase_times(None, None) == _lib.FSA_ERR_INVALID_ARGUMENT
+
+
+def test_sharded_entry_points_reject_bad_tables_before_cuda():
+    import ctypes as C
+
+    two = (C.c_void_p * 2)(16, 32)
+    nul = (C.c_void_p * 2)(16, None)
+    # (table, shard_rows, num_shards, num_nodes): count, coverage, null, alignment
+    bad = [(two, 5, 0, 10), (two, 5, _lib.MAX_SHARDS + 1, 10), (two, 4, 2, 10),
+           (nul, 5, 2, 10), ((C.c_void_p * 2)(16, 36), 5, 2, 10), (two, 0, 2, 10)]
+    for table, rows, n, nodes in bad:
+        assert L.fsa_sample_agg_2hop_forward_sharded(
+            NULL, NULL, nodes, 10, table, rows, n, 4, NULL, 5, 0, 3, 2, 1, NULL, NULL, NULL,
+            NULL, 0, NULL, 0, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+        assert L.fsa_sample_agg_2hop_backward_sharded(
+            NULL, NULL, NULL, 5, 4, 3, 2, table, rows, n, nodes,
+            NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+
+
+def test_ipc_and_peer_helpers_reject_null_arguments():
+    assert L.fsa_ipc_export(NULL, NULL, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert L.fsa_ipc_open(NULL, 0, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert L.fsa_ipc_close(NULL, 0) == _lib.FSA_ERR_INVALID_ARGUMENT
