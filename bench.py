@@ -655,7 +655,10 @@ def run(args) -> None:
             "fill": "fsa_fill_zero_kernel (stand-alone zero fill, not in the step)",
         }
         kernels = {}
-        for name in ("plan", "scan", "draw", "gather", "bwd", "fill"):
+        launched = ["plan", "draw", "gather", "bwd", "fill"]
+        if inp.B >= 2048:  # smaller batches are scanned inside the draw kernel
+            launched.insert(1, "scan")
+        for name in launched:
             us = kt["fill_alone"] if name == "fill" else kt[name]
             achieved = bytes_model[name] / (us * 1e-6) / 1e9
             kernels[name] = {
@@ -669,7 +672,7 @@ def run(args) -> None:
         kernels["draw"]["rng_draws_per_launch"] = bytes_model["rng_draws"]
         kernels["draw"]["rng_draws_per_s"] = bytes_model["rng_draws"] / (kt["draw"] * 1e-6)
         kernels["forward_without_fill_us"] = kt["fwd_nofill"]
-        dom = max(("plan", "scan", "draw", "gather", "bwd"), key=lambda k: kt[k])
+        dom = max((k for k in launched if k != "fill"), key=lambda k: kt[k])
         traffic = NCU_TRAFFIC.get(args.workload, {}).get(dom)
         result["roofline"] = {
             "kernel": kernels[dom]["kernel"],
