@@ -194,39 +194,4 @@ inline uint64_t chunk_start_host(const JumpTables& jt, const LaneTables& k1,
   return s;
 }
 
-// Multipliers 2^20, 2^25 and 2^5, passed as kernel arguments so that the
-// compiler keeps the shifts below as integer multiplies (FMA pipe) instead
-// of turning them back into shift instructions (ALU pipe): the draw loop is
-// otherwise bound by the ALU pipe, which also executes every XOR.
-struct ShiftMultipliers {
-  uint32_t m20, m25, m5;
-};
-
-constexpr ShiftMultipliers kShiftMultipliers{1u << 20, 1u << 25, 1u << 5};
-
-FSA_HD uint32_t mulhi32(uint32_t a, uint32_t b) {
-#if defined(__CUDA_ARCH__)
-  return __umulhi(a, b);
-#else
-  return static_cast<uint32_t>((static_cast<uint64_t>(a) * b) >> 32);
-#endif
-}
-
-// One xorshift64 step on 32-bit halves:
-//   s >> 12: hi*2^20 gives (hi >> 12 : hi << 20); lo >> 12 = mulhi(lo, 2^20)
-//   s << 25: lo*2^25 gives (lo >> 7 : lo << 25);  hi << 25 = hi * 2^25
-//   s >> 27: hi*2^5  gives (hi >> 27 : hi << 5);  lo >> 27 = mulhi(lo, 2^5)
-// The two parts of each shifted half never overlap, so adding them is OR.
-FSA_HD void xorshift_step_mul(uint32_t& lo, uint32_t& hi, const ShiftMultipliers& m) {
-  uint64_t t = static_cast<uint64_t>(hi) * m.m20;
-  lo ^= mulhi32(lo, m.m20) + static_cast<uint32_t>(t);
-  hi ^= static_cast<uint32_t>(t >> 32);
-  t = static_cast<uint64_t>(lo) * m.m25;
-  hi ^= hi * m.m25 + static_cast<uint32_t>(t >> 32);
-  lo ^= static_cast<uint32_t>(t);
-  t = static_cast<uint64_t>(hi) * m.m5;
-  lo ^= mulhi32(lo, m.m5) + static_cast<uint32_t>(t);
-  hi ^= static_cast<uint32_t>(t >> 32);
-}
-
 }  // namespace fsa

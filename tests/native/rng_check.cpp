@@ -37,11 +37,6 @@ int main() {
                                  fsa::chunk_start_host(kTables, kLanes1, kLanes2, a, b)));
     } else if (std::strcmp(op, "chunkt") == 0) {
       std::printf("%llu\n", static_cast<unsigned long long>(chunk_start_transposed(a, b)));
-    } else if (std::strcmp(op, "stepmul") == 0) {
-      // b steps with the multiply form of the xorshift step
-      uint32_t lo = static_cast<uint32_t>(a), hi = static_cast<uint32_t>(a >> 32);
-      for (unsigned long long k = 0; k < b; ++k) fsa::xorshift_step_mul(lo, hi, fsa::kShiftMultipliers);
-      std::printf("%llu\n", (static_cast<unsigned long long>(hi) << 32) | lo);
     } else if (std::strcmp(op, "draw") == 0) {
       std::printf("%u\n", fsa::bounded_draw(a, static_cast<uint32_t>(b)));
     } else if (std::strcmp(op, "seed") == 0) {

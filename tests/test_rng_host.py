@@ -89,12 +89,3 @@ def test_chunk_start_equals_serial_steps(run):
     assert got == want
     # the 2-hop draw kernel's form (one-chunk tables with the lane innermost)
     assert run([f"chunkt {s} {j}" for s, j in cases]) == want
-
-
-def test_multiply_form_of_xorshift_step(run):
-    rng = random.Random(6)
-    cases = [(rng.getrandbits(64), n) for n in (1, 2, 3, 10, 1000)]
-    cases += [(U64, 5), (1, 7), (1 << 63, 3), (0x9E3779B97F4A7C15, 64)]
-    got = run([f"stepmul {s} {n}" for s, n in cases])
-    want = [str(oracle.xorshift_advance(s, n)) for s, n in cases]
-    assert got == want
