@@ -74,6 +74,22 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+# The process's stdout carries exactly one JSON line.  Libraries write to
+# file descriptor 1 on their own (NCCL's version banner, for one), so main()
+# points descriptor 1 at stderr and the result goes to a saved copy of the
+# original stdout.
+_RESULT_FD = None
+
+
+def emit(obj) -> None:
+    data = json.dumps(obj) + "\n"
+    if _RESULT_FD is None:
+        sys.stdout.write(data)
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, data.encode())
+
+
 # ---------------------------------------------------------------------------
 # Distributed plumbing
 # ---------------------------------------------------------------------------
@@ -89,9 +105,6 @@ class Dist:
         if self.world > 1 and not self.pg:
             import torch.distributed as dist
 
-            # rank 0's stdout carries exactly one JSON line: keep NCCL's
-            # version banner off it unless the caller asked for NCCL logs
-            os.environ.setdefault("NCCL_DEBUG", "WARN")
 
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local_rank))
@@ -558,9 +571,9 @@ def run(args) -> None:
         api = load_reference_op()
         if api is None:
             if dist.rank == 0:
-                print(json.dumps({"impl": "reference",
-                                  "unavailable": "reference op not built into oracle/_ref "
-                                                 "(python -m oracle.build --ref)"}))
+                emit({"impl": "reference",
+                      "unavailable": "reference op not built into oracle/_ref "
+                                     "(python -m oracle.build --ref)"})
             dist.close()
             return
     batches = args.batches
@@ -594,6 +607,7 @@ def run(args) -> None:
     value = units / (ms / 1000.0)
     e2e_value = units / (e2e_ms / 1000.0)
     used = sorted({(args.warmup + i) % batches for i in range(args.steps)})
+    torch.cuda.empty_cache()  # the steps' cached gradient buffers (51 GB each on C5)
     bytes_model = byte_model(w, inp, used[: min(len(used), 16)]) if feats is None else None
     peak, peak_kind = load_peaks()
     if feats is not None:
@@ -644,6 +658,7 @@ def run(args) -> None:
         result["mode"] = "sharded"
         result["gpu_launches"] = launches
     elif args.impl == "ours":
+        torch.cuda.empty_cache()
         kt = kernel_times(w, inp, iters=min(args.steps, 30))
         names = {
             "plan": "fsa_2hop_plan_kernel (first hop, second-hop row table)",
@@ -699,7 +714,7 @@ def run(args) -> None:
         result["cpu_baseline"] = None
     dist.close()
     if dist.rank == 0:
-        print(json.dumps(result))
+        emit(result)
 
 
 def profile_forward(args) -> None:
@@ -738,11 +753,15 @@ def profile_forward(args) -> None:
                 inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
                 grad.data_ptr(), n, stream), "bwd")
     torch.cuda.synchronize()
-    print(json.dumps({"profile_forward": args.profile_forward, "calls": args.calls,
-                      "workload": args.workload}))
+    emit({"profile_forward": args.profile_forward, "calls": args.calls,
+          "workload": args.workload})
 
 
 def main() -> None:
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=1000)
