@@ -443,7 +443,16 @@ def kernel_times(w, inp: Inputs, iters: int) -> dict:
         fwd(it % nb, True)
         bwd()
     torch.cuda.synchronize()
-    res = {"bwd": 0.0, "fwd_nofill": 0.0, "fill_alone": 0.0}
+    res = {"bwd": 0.0, "bwd_sorted": 0.0, "fwd_nofill": 0.0, "fill_alone": 0.0}
+    sws_bytes = L.fsa_sample_agg_2hop_backward_sorted_workspace_size(n, B, k1, k2)
+    sws = torch.empty((sws_bytes,), dtype=torch.uint8, device=dev)
+
+    def bwd_sorted():
+        _lib.check(L.fsa_sample_agg_2hop_backward_sorted(
+            inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
+            grad.data_ptr(), n, sws.data_ptr(), sws_bytes, stream), "bwd_sorted")
+
+    bwd_sorted()
     _lib.phase_timing(True)
     try:
         for it in range(iters):
@@ -457,6 +466,15 @@ def kernel_times(w, inp: Inputs, iters: int) -> dict:
         phases, calls = _lib.phase_times()
     finally:
         _lib.phase_timing(False)
+    for it in range(iters):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        fwd(it % nb, True)
+        ev[0].record()
+        bwd_sorted()
+        ev[1].record()
+        torch.cuda.synchronize()
+        res["bwd_sorted"] += ev[0].elapsed_time(ev[1])
+    del sws
     for it in range(iters):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record()
@@ -687,6 +705,13 @@ def run(args) -> None:
         kernels["draw"]["rng_draws_per_launch"] = bytes_model["rng_draws"]
         kernels["draw"]["rng_draws_per_s"] = bytes_model["rng_draws"] / (kt["draw"] * 1e-6)
         kernels["forward_without_fill_us"] = kt["fwd_nofill"]
+        kernels["bwd_sorted_alternative"] = {
+            "kernels": "fsa_2hop_sortbwd_{count,scatter,reduce}_kernel + fsa_sortbwd_scan_"
+                       "{tiles,totals}_kernel + counts zero fill (sort-by-destination "
+                       "backward, not in the step)",
+            "avg_us": kt["bwd_sorted"],
+            "vs_atomic_bwd": kt["bwd_sorted"] / kt["bwd"],
+        }
         dom = max((k for k in launched if k != "fill"), key=lambda k: kt[k])
         traffic = NCU_TRAFFIC.get(args.workload, {}).get(dom)
         result["roofline"] = {
@@ -722,7 +747,8 @@ def profile_forward(args) -> None:
     `--calls` 2-hop forwards of the workload (different root batches), each
     followed by its backward; `--profile-forward fused` zeroes the gradient
     inside the forward (the step's configuration), `separate` with the
-    stand-alone fill kernel, `none` runs forwards only."""
+    stand-alone fill kernel, `none` runs forwards only.  `--backward sorted`
+    runs the sort-by-destination backward instead of the atomic one."""
     from fusesampleagg_b200 import _lib
 
     dev = torch.device("cuda", 0)
@@ -740,6 +766,9 @@ def profile_forward(args) -> None:
     ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
     fused = args.profile_forward == "fused"
+    if args.backward == "sorted":
+        sws_bytes = L.fsa_sample_agg_2hop_backward_sorted_workspace_size(n, B, k1, k2)
+        sws = torch.empty((sws_bytes,), dtype=torch.uint8, device=dev)
     for j in range(args.calls):
         if args.profile_forward == "separate":
             _lib.check(L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fill")
@@ -748,13 +777,17 @@ def profile_forward(args) -> None:
             inp.frontiers[j].data_ptr(), B, 0, k1, k2, inp.seeds[j], out.data_ptr(),
             s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes,
             grad.data_ptr() if fused else None, grad.numel() if fused else 0, stream), "fwd")
-        if grad is not None:
+        if grad is not None and args.backward == "sorted":
+            _lib.check(L.fsa_sample_agg_2hop_backward_sorted(
+                inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
+                grad.data_ptr(), n, sws.data_ptr(), sws_bytes, stream), "bwd_sorted")
+        elif grad is not None:
             _lib.check(L.fsa_sample_agg_2hop_backward(
                 inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
                 grad.data_ptr(), n, stream), "bwd")
     torch.cuda.synchronize()
     emit({"profile_forward": args.profile_forward, "calls": args.calls,
-          "workload": args.workload})
+          "backward": args.backward, "workload": args.workload})
 
 
 def main() -> None:
@@ -777,6 +810,8 @@ def main() -> None:
     p.add_argument("--profile-forward", choices=["fused", "separate", "none"],
                    help="run a short C-ABI call sequence for ncu instead of the benchmark")
     p.add_argument("--calls", type=int, default=3, help="calls of --profile-forward")
+    p.add_argument("--backward", choices=["atomic", "sorted"], default="atomic",
+                   help="backward variant of --profile-forward")
     args = p.parse_args()
     if args.profile_forward:
         profile_forward(args)

@@ -52,6 +52,10 @@ SIGNATURES = {
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, ctypes.POINTER(_p), _i64, _i32, _i64, _p]),
     "fsa_sample_agg_2hop_backward": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p]),
+    "fsa_sample_agg_2hop_backward_sorted_workspace_size": (ctypes.c_size_t,
+                                                            [_i64, _i64, _i32, _i32]),
+    "fsa_sample_agg_2hop_backward_sorted": (
+        _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p, ctypes.c_size_t, _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),
     "fsa_phase_timing": (_int, [_int]),
     "fsa_phase_times": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),

@@ -800,8 +800,11 @@ __host__ __device__ inline LayoutG layout_gather(int k1, int k2, int dchunk) {
   return l;
 }
 
-// Rows gathered per batch of independent loads (per thread).
-constexpr int kGatherBatch = 8;
+// Rows gathered per batch of independent loads (per thread): a whole
+// second-hop row of fanout 10 in one round trip.  Measured against 4, 6
+// and 8 (with more CTAs per SM): 10 at 4 CTAs per SM was fastest on the
+// 2-hop power-law and 1M-node microbenchmark workloads.
+constexpr int kGatherBatch = 10;
 
 // CTA per root.  Items are (first-hop slot, feature vector) pairs: an item
 // sums its slot's valid leaf rows in j order from 0.0f (loads batched so
@@ -809,7 +812,7 @@ constexpr int kGatherBatch = 8;
 // count; then the slot means are summed in slot order and divided by the
 // non-empty count (fused_sample_agg.cu:189-213).
 template <int V, bool kSharded>
-__global__ void __launch_bounds__(kThreadsGather)
+__global__ void __launch_bounds__(kThreadsGather, 4)
     fsa_2hop_gather_kernel(const Gather2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int k1 = a.fanout1;
@@ -1024,6 +1027,158 @@ __global__ void __launch_bounds__(kThreadsBwd)
       }
     }
     __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Sort-by-destination 2-hop backward (the alternative to red.global.add):
+// contributions are grouped by destination row with a counting sort, then
+// one warp per destination row sums them and writes the row once -- no
+// atomics on the gradient, one write per touched row.
+// ---------------------------------------------------------------------------
+
+struct SortBwdArgs {
+  const float* grad_out;
+  const int32_t* samples1;
+  const int32_t* samples2;
+  int64_t batch_size;
+  int64_t feature_dim;
+  int fanout1;
+  int fanout2;
+  float* grad_x;
+  int64_t num_nodes;
+  int32_t* counts;      // [N + 1] entries per destination row, then the valid-entry
+                        // total; zero on entry, zero again after the scatter
+  int32_t* offsets;     // [N] exclusive prefix of counts
+  long long* bsum;      // [ceil(N / kSortTile) + 1] tile totals, then their prefix
+  int32_t* skey;        // [E] destination row of each sorted entry
+  int32_t* sval;        // [E] (root, slot) = b * k1 + i of each sorted entry
+  int32_t* slot_valid;  // [B * k1] valid second-hop ids of each slot
+  int32_t* nonempty;    // [B] non-empty slots of each root
+  int32_t* nentries;    // = counts + N: valid entries (the sorted length)
+};
+
+constexpr int kThreadsSort = 1024;
+constexpr int kSortItems = 4;
+constexpr int kSortTile = kThreadsSort * kSortItems;
+static_assert(kSortItems == kScanItems, "one scan tile per CTA");
+
+// Per root: valid count of every slot, the non-empty count (a slot counts
+// when its first-hop id is valid and it has a valid second-hop id,
+// fused_sample_agg.cu:229-240), and the histogram of destination rows.
+__global__ void __launch_bounds__(256) fsa_2hop_sortbwd_count_kernel(const SortBwdArgs a) {
+  __shared__ int ne;
+  const int k1 = a.fanout1;
+  const int k2 = a.fanout2;
+  for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
+    if (threadIdx.x == 0) ne = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < k1; i += blockDim.x) {
+      int cnt = 0;
+      for (int j = 0; j < k2; ++j) {
+        const int32_t leaf = a.samples2[(b * k1 + i) * k2 + j];
+        if (leaf >= 0) {
+          ++cnt;
+          if (leaf < a.num_nodes) {
+            atomicAdd(a.counts + leaf, 1);
+            atomicAdd(a.nentries, 1);
+          } else {
+            flag_status(FSA_STATUS_BAD_NEIGHBOR);
+          }
+        }
+      }
+      a.slot_valid[b * k1 + i] = cnt;
+      if (cnt > 0 && a.samples1[b * k1 + i] >= 0) atomicAdd(&ne, 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) a.nonempty[b] = ne;
+    __syncthreads();
+  }
+}
+
+// Tile-local exclusive prefix of counts into offsets; tile totals to bsum.
+__global__ void __launch_bounds__(kThreadsSort) fsa_sortbwd_scan_tiles_kernel(const SortBwdArgs a) {
+  __shared__ long long warp_sums[32];
+  __shared__ long long carry;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kSortTile;
+  const int64_t n = a.num_nodes - t0 < kSortTile ? a.num_nodes - t0 : kSortTile;
+  // block_exclusive_scan works on long long; scan this tile through a
+  // shared copy.
+  __shared__ long long vals[kSortTile + 1];
+  for (int64_t t = threadIdx.x; t < n; t += blockDim.x) vals[t] = a.counts[t0 + t];
+  __syncthreads();
+  block_exclusive_scan(vals, vals, n, warp_sums, &carry);
+  for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
+    a.offsets[t0 + t] = static_cast<int32_t>(vals[t]);
+  }
+  if (threadIdx.x == 0) a.bsum[blockIdx.x] = vals[n];
+}
+
+// Exclusive prefix of the tile totals (one CTA), in place in global memory
+// (every tile's reads precede its writes in block_exclusive_scan).
+__global__ void __launch_bounds__(kThreadsSort) fsa_sortbwd_scan_totals_kernel(
+    const SortBwdArgs a, int64_t tiles) {
+  __shared__ long long warp_sums[32];
+  __shared__ long long carry;
+  block_exclusive_scan(a.bsum, a.bsum, tiles, warp_sums, &carry);
+}
+
+// Every valid entry to its place: destination row's start + a slot claimed
+// by decrementing its count (the counts end at zero).
+__global__ void __launch_bounds__(256) fsa_2hop_sortbwd_scatter_kernel(const SortBwdArgs a) {
+  const int k1 = a.fanout1;
+  const int k2 = a.fanout2;
+  const int64_t total = a.batch_size * k1 * k2;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t leaf = a.samples2[e];
+    if (leaf < 0 || leaf >= a.num_nodes) continue;
+    const int32_t start = a.offsets[leaf] + static_cast<int32_t>(a.bsum[leaf / kSortTile]);
+    const int32_t pos = start + atomicSub(a.counts + leaf, 1) - 1;
+    a.skey[pos] = leaf;
+    a.sval[pos] = static_cast<int32_t>(e / k2);
+  }
+}
+
+// One warp per run of equal destinations in the sorted order: lanes over
+// feature vectors add ((g / nonempty) / valid) of the run's entries (the
+// reference's per-entry arithmetic, fused_sample_agg.cu:247-260) to the
+// row's current value and store it once (no atomics).
+template <int V>
+__global__ void __launch_bounds__(256) fsa_2hop_sortbwd_reduce_kernel(const SortBwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int k1 = a.fanout1;
+  const int64_t D = a.feature_dim;
+  const int64_t dvec = D / V;
+  const int64_t E = *a.nentries;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w0 = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 32;
+       w0 < E; w0 += warps * 32) {
+    const int64_t p = w0 + lane;
+    const bool head = p < E && (p == 0 || a.skey[p] != a.skey[p - 1]);
+    unsigned heads = __ballot_sync(0xffffffffU, head);
+    while (heads != 0) {
+      const int h = __ffs(heads) - 1;
+      heads &= heads - 1;
+      const int64_t s0 = w0 + h;
+      const int32_t leaf = a.skey[s0];
+      float* row = a.grad_x + static_cast<int64_t>(leaf) * D;
+      for (int64_t v = lane; v < dvec; v += 32) {
+        VecF<V> acc = load_vec<V>(row + v * V);
+        for (int64_t q = s0; q < E && a.skey[q] == leaf; ++q) {
+          const int32_t bi = a.sval[q];
+          const int64_t b = bi / k1;
+          const int nonempty = a.nonempty[b];
+          if (nonempty == 0) continue;  // the atomic variant skips such roots too
+          const float ne = static_cast<float>(nonempty);
+          const float vc = static_cast<float>(a.slot_valid[bi]);
+          const VecF<V> g = load_vec<V>(a.grad_out + b * D + v * V);
+#pragma unroll
+          for (int c = 0; c < V; ++c) acc.v[c] += (g.v[c] / ne) / vc;
+        }
+        store_vec(row + v * V, acc);
+      }
+    }
   }
 }
 
@@ -1507,6 +1662,90 @@ int fsa_sample_agg_2hop_backward_sharded(const float* grad_out, const int32_t* s
   if (st != FSA_OK) return st;
   return backward_2hop(grad_out, samples1, samples2, batch_size, feature_dim, fanout1, fanout2,
                        t.base[0], num_nodes, stream, &t);
+}
+
+// Workspace of the sort-by-destination backward, in bytes from a 256-byte
+// aligned base.
+struct WsSort {
+  size_t counts, offsets, bsum, skey, sval, slot_valid, nonempty, total;
+};
+
+static WsSort ws_sort_layout(int64_t N, int64_t B, int k1, int k2) {
+  WsSort l{};
+  const size_t E = static_cast<size_t>(B) * k1 * k2;
+  const size_t tiles = static_cast<size_t>((N + kSortTile - 1) / kSortTile);
+  size_t off = 0;
+  l.counts = off;     off = align256(off + 4 * (static_cast<size_t>(N) + 1));
+  l.offsets = off;    off = align256(off + 4 * static_cast<size_t>(N));
+  l.bsum = off;       off = align256(off + 8 * (tiles + 1));
+  l.skey = off;       off = align256(off + 4 * E);
+  l.sval = off;       off = align256(off + 4 * E);
+  l.slot_valid = off; off = align256(off + 4 * static_cast<size_t>(B) * k1);
+  l.nonempty = off;   off = align256(off + 4 * static_cast<size_t>(B));
+  l.total = off;
+  return l;
+}
+
+size_t fsa_sample_agg_2hop_backward_sorted_workspace_size(int64_t num_nodes, int64_t batch_size,
+                                                          int32_t fanout1, int32_t fanout2) {
+  if (num_nodes < 0 || batch_size <= 0 || fanout1 <= 0 || fanout2 <= 0) return 0;
+  return ws_sort_layout(num_nodes, batch_size, fanout1, fanout2).total;
+}
+
+int fsa_sample_agg_2hop_backward_sorted(const float* grad_out, const int32_t* samples1,
+                                        const int32_t* samples2, int64_t batch_size,
+                                        int64_t feature_dim, int32_t fanout1, int32_t fanout2,
+                                        float* grad_x, int64_t num_nodes, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (fanout1 < 0 || fanout2 < 0 || batch_size < 0 || feature_dim < 0 || num_nodes < 0) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  if (static_cast<int64_t>(fanout1) + static_cast<int64_t>(fanout1) * fanout2 >
+      FSA_MAX_2HOP_ENTRIES) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  if (batch_size == 0 || fanout1 == 0 || fanout2 == 0 || feature_dim == 0 || num_nodes == 0) {
+    return FSA_OK;
+  }
+  const int64_t E = batch_size * fanout1 * fanout2;
+  const WsSort wl = ws_sort_layout(num_nodes, batch_size, fanout1, fanout2);
+  if (grad_out == nullptr || samples1 == nullptr || samples2 == nullptr || grad_x == nullptr ||
+      workspace == nullptr || workspace_bytes < wl.total || !aligned(workspace, 256) ||
+      E > 0x7fffffffLL || num_nodes > 0x7fffffffLL) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  char* ws = static_cast<char*>(workspace);
+  SortBwdArgs a{grad_out, samples1, samples2, batch_size, feature_dim, fanout1, fanout2, grad_x,
+                num_nodes,
+                reinterpret_cast<int32_t*>(ws + wl.counts),
+                reinterpret_cast<int32_t*>(ws + wl.offsets),
+                reinterpret_cast<long long*>(ws + wl.bsum),
+                reinterpret_cast<int32_t*>(ws + wl.skey),
+                reinterpret_cast<int32_t*>(ws + wl.sval),
+                reinterpret_cast<int32_t*>(ws + wl.slot_valid),
+                reinterpret_cast<int32_t*>(ws + wl.nonempty),
+                reinterpret_cast<int32_t*>(ws + wl.counts) + num_nodes};
+  auto s = static_cast<cudaStream_t>(stream);
+  // counts and the entry total start at zero (int32 zero = float zero bits)
+  int st = fsa_fill_zero_f32(reinterpret_cast<float*>(a.counts), num_nodes + 1, stream);
+  if (st != FSA_OK) return st;
+  st = launch(fsa_2hop_sortbwd_count_kernel, grid_for(batch_size), 256, 0, s, a);
+  if (st != FSA_OK) return st;
+  const int64_t tiles = (num_nodes + kSortTile - 1) / kSortTile;
+  st = launch(fsa_sortbwd_scan_tiles_kernel, static_cast<int>(tiles), kThreadsSort, 0, s, a);
+  if (st != FSA_OK) return st;
+  fsa_sortbwd_scan_totals_kernel<<<1, kThreadsSort, 0, s>>>(a, tiles);
+  st = check_launch();
+  if (st != FSA_OK) return st;
+  st = launch(fsa_2hop_sortbwd_scatter_kernel, grid_for((E + 255) / 256), 256, 0, s, a);
+  if (st != FSA_OK) return st;
+  const int vec = pick_vec(feature_dim, grad_out, grad_x);
+  const int rgrid = grid_for((E + 255) / 256);
+  switch (vec) {
+    case 4: return launch(fsa_2hop_sortbwd_reduce_kernel<4>, rgrid, 256, 0, s, a);
+    case 2: return launch(fsa_2hop_sortbwd_reduce_kernel<2>, rgrid, 256, 0, s, a);
+    default: return launch(fsa_2hop_sortbwd_reduce_kernel<1>, rgrid, 256, 0, s, a);
+  }
 }
 
 int fsa_fill_zero_f32(float* dst, int64_t count, void* stream) {

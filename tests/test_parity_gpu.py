@@ -343,3 +343,57 @@ def test_bad_neighbor_and_bad_row_are_flagged():
     flags = fsa.device_status(reset=True)
     assert flags & 0x2 and flags & 0x4
     assert torch.isfinite(out).all()
+
+
+# ---------------------------------------------------------------------------
+# Sort-by-destination backward (alternative to the atomic scatter)
+# ---------------------------------------------------------------------------
+
+def sorted_backward(go, s1, s2, num_nodes, base=None):
+    from fusesampleagg_b200 import _lib
+
+    L = _lib.LIB
+    B, D = go.shape
+    k1, k2 = s1.size(1), s2.size(2)
+    grad = (base.clone() if base is not None
+            else torch.zeros((num_nodes, D), device=go.device))
+    nbytes = L.fsa_sample_agg_2hop_backward_sorted_workspace_size(num_nodes, B, k1, k2)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=go.device)
+    _lib.check(L.fsa_sample_agg_2hop_backward_sorted(
+        go.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2, grad.data_ptr(), num_nodes,
+        ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream), "sorted backward")
+    return grad
+
+
+@pytest.mark.parametrize("name,fan,dim", [("toy", (3, 2), 19), ("powerlaw", (15, 10), 100),
+                                          ("hub", (5, 10), 33), ("powerlaw", (8, 4), 2),
+                                          ("uniform", (25, 10), 64)])
+def test_sorted_backward_matches_oracle(name, fan, dim):
+    g = cpu_graph(name)
+    out, s1, s2, _, r1, r2 = run_2hop(name, fan[0], fan[1], 7, dim=dim, batch=96)
+    go = synthetic.features(s1.size(0), dim, seed=4)
+    grad = sorted_backward(go.cuda(), s1, s2, g.num_nodes)
+    ref = oracle.backward_2hop(go.numpy(), r1, r2, g.num_nodes)
+    np.testing.assert_allclose(grad.cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
+
+
+def test_sorted_backward_accumulates_and_matches_atomic_variant():
+    g = cpu_graph("powerlaw")
+    out, s1, s2, _, _, _ = run_2hop("powerlaw", 15, 10, 9, dim=64, batch=256)
+    go = synthetic.features(s1.size(0), 64, seed=5).cuda()
+    base = synthetic.features(g.num_nodes, 64, seed=6).cuda()
+    got = sorted_backward(go, s1, s2, g.num_nodes, base=base)
+    want = fsa._backward_2hop(go, s1, s2, g.num_nodes, zeroed=base.clone())
+    torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
+
+
+def test_sorted_backward_on_c2_graph_matches_atomic_variant():
+    w = synthetic.WORKLOADS["c2_2hop_powerlaw"]
+    g = w.graph(0, "cuda")
+    x = w.features(1, "cuda")
+    fr = synthetic.root_batch(g.num_nodes, 1024, 3, device="cuda")
+    _, s1, s2 = fsa.fused_sample_agg_2hop_with_samples(g.rowptr, g.col, x, fr, 15, 10, 3)
+    go = synthetic.features(1024, w.dim, seed=2, device="cuda")
+    got = sorted_backward(go, s1, s2, g.num_nodes)
+    want = fsa._backward_2hop(go, s1, s2, g.num_nodes)
+    torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
