@@ -310,60 +310,73 @@ def make_step(api, w, inp: Inputs, batch_offset: bool):
 
 def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
     """Public-API step with host buffers: every step copies its roots and
-    upstream gradient from pinned host memory and reads its output back into
-    pinned memory.  As a data loader would, the copies run on a second
-    stream: step i's inputs are copied while step i-1 computes (double
-    buffered), and step i's output is read back while step i+1 computes.
-    `reset()` drops the prefetched inputs, so the first step after it copies
-    its own inputs before computing."""
+    upstream gradient from pinned host memory (one packed buffer per root
+    batch, one copy) and reads its output back into pinned memory.  As a
+    data loader would, the copies run on a second stream: step i+1's inputs
+    are copied while step i computes (double buffered), and step i's output
+    is read back while step i+1 computes.  `reset()` drops the prefetched
+    inputs, so the first step after it copies its own inputs first."""
     k1, k2 = w.fanouts
     nb = len(inp.frontiers)
     kw = {"batch_offset": inp.offset} if batch_offset else {}
     dev = inp.x.device
-    host_fr = [f.cpu().pin_memory() for f in inp.frontiers]
-    host_go = inp.grad_out.cpu().pin_memory()
+    fr_bytes = inp.frontiers[0].numel() * 4
+    go_bytes = inp.grad_out.numel() * 4
+    nbytes = fr_bytes + go_bytes
+    go_u8 = inp.grad_out.reshape(-1).view(torch.uint8).cpu()
+    host_in = []
+    for f in inp.frontiers:
+        h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        h[:fr_bytes].copy_(f.cpu().view(torch.uint8))
+        h[fr_bytes:].copy_(go_u8)
+        host_in.append(h)
     host_out = [torch.empty((w.batch, w.dim), dtype=torch.float32).pin_memory() for _ in range(2)]
-    dev_fr = [torch.empty_like(inp.frontiers[0]) for _ in range(2)]
-    dev_go = [torch.empty_like(inp.grad_out) for _ in range(2)]
+    dev_in = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    dev_fr = [b[:fr_bytes].view(torch.int32) for b in dev_in]
+    dev_go = [b[fr_bytes:].view(torch.float32).view(w.batch, w.dim) for b in dev_in]
     copy = torch.cuda.Stream(device=dev)
     free = [None, None]       # event after the last compute that read a slot
-    prefetched = {}           # step -> event of its input copies
-    h2d = host_fr[0].numel() * 4 + host_go.numel() * 4
+    ready = {}                # step -> event of its input copy
     d2h = host_out[0].numel() * 4
+    # Events are reused two steps later: by then every wait on their previous
+    # record has been enqueued (a wait binds to the record it sees).
+    ready_ev = [torch.cuda.Event() for _ in range(2)]
+    done_ev = [torch.cuda.Event() for _ in range(2)]
 
     def copy_inputs(i):
+        # on the copy stream
         slot = i % 2
-        with torch.cuda.stream(copy):
-            if free[slot] is not None:
-                copy.wait_event(free[slot])
-            dev_fr[slot].copy_(host_fr[i % nb], non_blocking=True)
-            dev_go[slot].copy_(host_go, non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(copy)
-        return ev
+        if free[slot] is not None:
+            copy.wait_event(free[slot])
+        dev_in[slot].copy_(host_in[i % nb], non_blocking=True)
+        ev = ready_ev[slot]
+        ev.record(copy)
+        ready[i] = ev
 
     def step(i):
         comp = torch.cuda.current_stream()
         slot = i % 2
-        ready = prefetched.pop(i, None) or copy_inputs(i)
-        comp.wait_event(ready)
-        prefetched[i + 1] = copy_inputs(i + 1)
+        if i not in ready:
+            with torch.cuda.stream(copy):
+                copy_inputs(i)
+        comp.wait_event(ready.pop(i))
         inp.x.grad = None
         out = api.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, dev_fr[slot], k1, k2,
                                         replay_seed=inp.seeds[i % nb], **kw)
         out.backward(dev_go[slot])
-        done = torch.cuda.Event()
+        done = done_ev[slot]
         done.record(comp)
         free[slot] = done
         with torch.cuda.stream(copy):
+            copy_inputs(i + 1)          # does not wait for this step's compute
             copy.wait_event(done)
             host_out[slot].copy_(out.detach(), non_blocking=True)
         out.record_stream(copy)
 
-    step.reset = prefetched.clear
+    step.reset = ready.clear
     # the last output read-back belongs to the timed region
     step.drain = lambda: torch.cuda.current_stream().wait_stream(copy)
-    return step, h2d, d2h
+    return step, nbytes, d2h
 
 
 def timed(step, steps: int, warmup: int, dist: Dist, sampler=None, phase_events=False):
@@ -667,9 +680,10 @@ def run(args) -> None:
         "phases_ms": phases,
         "e2e": {"value": e2e_value, "unit": "roots/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "copies": "roots + upstream gradient H2D from pinned memory one step ahead "
-                          "on a copy stream (double-buffered), output D2H into pinned memory "
-                          "overlapping the next step; first step copies its own inputs"},
+                "copies": "roots + upstream gradient packed in one pinned buffer per root "
+                          "batch, one H2D per step issued one step ahead on a copy stream "
+                          "(double-buffered), output D2H into pinned memory overlapping the "
+                          "next step; the first timed step copies its own inputs"},
         "clocks": clocks,
     }
     if feats is not None:

@@ -53,18 +53,20 @@ def _check_python_inputs(rowptr, col, x, frontier) -> None:
 
 
 def _check_graph_inputs(rowptr, col, x, frontier) -> None:
-    tensors = (rowptr, col, x, frontier)
-    if not all(t.is_cuda for t in tensors):
+    dev = x.device
+    if not (x.is_cuda and rowptr.is_cuda and col.is_cuda and frontier.is_cuda):
         raise RuntimeError("all inputs must be CUDA tensors")
-    if not (rowptr.device == col.device == x.device == frontier.device):
+    if rowptr.device != dev or col.device != dev or frontier.device != dev:
         raise RuntimeError("all inputs must be on the same CUDA device")
-    if rowptr.dtype != torch.int32 or col.dtype != torch.int32 or frontier.dtype != torch.int32:
+    i32 = torch.int32
+    if rowptr.dtype != i32 or col.dtype != i32 or frontier.dtype != i32:
         raise RuntimeError("rowptr, col, and frontier must be int32")
     if x.dtype != torch.float32:
         raise RuntimeError("x must be float32")
     if rowptr.dim() != 1 or col.dim() != 1 or x.dim() != 2 or frontier.dim() != 1:
         raise RuntimeError("expected rowptr[N+1], col[E], x[N,D], and frontier[B]")
-    if not all(t.is_contiguous() for t in tensors):
+    if not (x.is_contiguous() and rowptr.is_contiguous() and col.is_contiguous()
+            and frontier.is_contiguous()):
         raise RuntimeError("all inputs must be contiguous")
     if rowptr.numel() != x.size(0) + 1:
         raise RuntimeError("rowptr length must equal N+1")
@@ -129,7 +131,16 @@ class _DeviceGuard:
         return False
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_handle(device: torch.device) -> int:
+    """cudaStream_t of the current stream of `device` (the raw-handle query
+    when this torch build has it: a fraction of the cost of building a
+    torch.cuda.Stream object on every call)."""
+    if _raw_stream is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -209,6 +220,20 @@ def _backward_1hop(samples, takes, grad_out, num_nodes):
     return grad_x
 
 
+_ws_sizes: dict = {}
+
+
+def _workspace_bytes_2hop(B: int, fanout1: int, fanout2: int, capture: bool) -> int:
+    key = (B, fanout1, fanout2, capture)
+    n = _ws_sizes.get(key)
+    if n is None:
+        if len(_ws_sizes) >= 1024:
+            _ws_sizes.clear()
+        n = _ws_sizes[key] = _L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2,
+                                                                   int(capture), int(capture))
+    return n
+
+
 def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, batch_offset=0,
                   zero=None):
     _check_graph_inputs(rowptr, col, x, frontier)
@@ -228,17 +253,28 @@ def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, bat
                 zero.zero_()
             return out, s1, s2
         out = torch.empty((B, D), dtype=x.dtype, device=dev)
-        s1 = torch.empty((B, fanout1), dtype=torch.int32, device=dev) if capture else None
-        s2 = torch.empty((B, fanout1, fanout2), dtype=torch.int32, device=dev) if capture else None
-        ws_bytes = _L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, int(capture),
-                                                         int(capture))
-        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+        ws_bytes = _workspace_bytes_2hop(B, fanout1, fanout2, capture)
+        if capture:
+            # samples1, samples2 and the workspace share one allocation, each
+            # part starting on a 256-byte boundary
+            n1 = B * fanout1
+            n2 = n1 * fanout2
+            o2 = (n1 + 63) // 64 * 64
+            ow = (o2 + n2 + 63) // 64 * 64
+            buf = torch.empty((ow + (ws_bytes + 3) // 4,), dtype=torch.int32, device=dev)
+            s1 = buf[:n1].view(B, fanout1)
+            s2 = buf[o2:o2 + n2].view(B, fanout1, fanout2)
+            ws_ptr = buf.data_ptr() + 4 * ow
+        else:
+            s1 = s2 = None
+            ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+            ws_ptr = ws.data_ptr()
         zero_ptr = zero.data_ptr() if zero is not None else None
         zero_count = zero.numel() if zero is not None else 0
         status = _L.fsa_sample_agg_2hop_forward(
             rowptr.data_ptr(), col.data_ptr(), x.size(0), col.numel(), x.data_ptr(), D,
             frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(), _ptr(s1),
-            _ptr(s2), ws.data_ptr(), ws_bytes, zero_ptr, zero_count, _stream_handle(dev))
+            _ptr(s2), ws_ptr, ws_bytes, zero_ptr, zero_count, _stream_handle(dev))
         _lib.check(status, "fsa_sample_agg_2hop_forward")
     return out, s1, s2
 
