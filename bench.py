@@ -105,7 +105,6 @@ class Dist:
         if self.world > 1 and not self.pg:
             import torch.distributed as dist
 
-
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local_rank))
             self.pg = True
@@ -379,6 +378,23 @@ def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
     return step, nbytes, d2h
 
 
+def with_gradient_allreduce(step, inp: Inputs):
+    """The step followed by the replicated mode's optional collective: an
+    NCCL all-reduce (sum) of the dense feature gradient over the ranks, on the
+    compute stream (`sharding.allreduce_gradient`)."""
+    from fusesampleagg_b200.sharding import allreduce_gradient
+
+    def run_step(i, *a):
+        out = step(i, *a)
+        allreduce_gradient(inp.x.grad)
+        return out
+
+    for attr in ("reset", "drain"):
+        if hasattr(step, attr):
+            setattr(run_step, attr, getattr(step, attr))
+    return run_step
+
+
 def timed(step, steps: int, warmup: int, dist: Dist, sampler=None, phase_events=False):
     for i in range(warmup):
         step(i)
@@ -620,6 +636,8 @@ def run(args) -> None:
         sampler.start()
     launches0 = api.launch_count() if args.impl == "ours" else None
     step = make_step(api, w, inp, batch_offset=args.impl == "ours")
+    if args.allreduce_grad:
+        step = with_gradient_allreduce(step, inp)
     ms, _ = timed(step, args.steps, args.warmup, dist, sampler)
     launches = (api.launch_count() - launches0) if args.impl == "ours" else None
     clocks = sampler.stop() if sampler else None
@@ -632,6 +650,8 @@ def run(args) -> None:
     _, phases = timed(step, min(args.steps, 100), args.warmup, dist, phase_events=True)
 
     e2e_step, h2d, d2h = make_e2e_step(api, w, inp, batch_offset=args.impl == "ours")
+    if args.allreduce_grad:
+        e2e_step = with_gradient_allreduce(e2e_step, inp)
     e2e_ms, _ = timed(e2e_step, args.steps, args.warmup, dist)
 
     units = w.batch * world * args.steps
@@ -672,6 +692,9 @@ def run(args) -> None:
                             "pointers; one-float NCCL all-reduce after forward and backward "
                             "as the cross-GPU ordering)" if feats is not None else
                             f"roots partitioned over {world} GPU(s), graph and features "
+                            "replicated, NCCL all-reduce (sum) of the dense N x D feature "
+                            "gradient after every backward" if args.allreduce_grad else
+                            f"roots partitioned over {world} GPU(s), graph and features "
                             "replicated, no data-path collective"),
             "l2": "inputs larger than L2: x (%.0f MB) gathered at random and the dense "
                   "gradient (%.0f MB) rewritten every step" % (
@@ -686,6 +709,8 @@ def run(args) -> None:
                           "next step; the first timed step copies its own inputs"},
         "clocks": clocks,
     }
+    if args.allreduce_grad:
+        result["mode"] = "replicated + gradient all-reduce"
     if feats is not None:
         result["mode"] = "sharded"
         result["gpu_launches"] = launches
@@ -821,6 +846,9 @@ def main() -> None:
     p.add_argument("--cpu-budget", type=float, default=12.0)
     p.add_argument("--sharded", action="store_true",
                    help="row-shard the features over the ranks (peer reads over NVLink)")
+    p.add_argument("--allreduce-grad", action="store_true",
+                   help="replicated features: all-reduce the dense feature gradient after "
+                        "every backward (NCCL)")
     p.add_argument("--profile-forward", choices=["fused", "separate", "none"],
                    help="run a short C-ABI call sequence for ncu instead of the benchmark")
     p.add_argument("--calls", type=int, default=3, help="calls of --profile-forward")
@@ -833,6 +861,9 @@ def main() -> None:
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.allreduce_grad and (args.sharded or args.impl != "ours" or ws == 1):
+        raise SystemExit("--allreduce-grad is the replicated mode's collective: this package "
+                         "on 2+ GPUs (torchrun)")
     if args.gpus != ws and ws != 1:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}")
     if args.gpus > 1 and ws == 1:

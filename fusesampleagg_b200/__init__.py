@@ -2,10 +2,11 @@
 
 Drop-in for the FuseSampleAgg Python API (fuseop/__init__.py:75-214): the
 same four functions with the same arguments, return containers, autograd
-saved-index replay and error types.  Every call goes through the C ABI of
-libfsa_sm100.so (include/fsa_sm100.h), which launches hand-written sm_100a
-kernels on the caller's current CUDA stream.  There is no CPU fallback: the
-import fails when the library is missing.
+saved-index replay and error types.  The autograd functions and output
+allocation live in a C++ torch binding (_fsa_torch, csrc/fsa_torch.cpp)
+that calls the C ABI of libfsa_sm100.so (include/fsa_sm100.h), which
+launches hand-written sm_100a kernels on the caller's current CUDA stream.
+There is no CPU fallback: the import fails when either is missing.
 
 Sampled neighbour ids are bit-identical to the reference for the same
 (graph, frontier, fanouts, replay_seed); forward outputs are bit-identical
@@ -23,6 +24,13 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+
+try:
+    from . import _fsa_torch as _C
+except ImportError as exc:  # no fallback: the binding is part of the build
+    raise ImportError(
+        "fusesampleagg_b200._fsa_torch is not built; run `python fusesampleagg_b200/build.py` "
+        f"before importing fusesampleagg_b200 ({exc})") from exc
 
 __all__ = [
     "fused_sample_agg",
@@ -311,76 +319,16 @@ def _backward_2hop(grad_out, samples1, samples2, num_nodes, zeroed=None):
 
 
 # ---------------------------------------------------------------------------
-# Autograd functions (fuseop/__init__.py:32-72, :108-161)
-# ---------------------------------------------------------------------------
-
-class _FusedSampleAggFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, rowptr, col, x, frontier, fanout, replay_seed, save_indices, batch_offset):
-        _check_python_inputs(rowptr, col, x, frontier)
-        capture = bool(save_indices) or x.requires_grad
-        out, samples, takes = _forward_1hop(
-            rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
-            fanout, replay_seed, capture, batch_offset)
-        if capture:
-            ctx.save_for_backward(samples, takes)
-            ctx.num_nodes = int(x.size(0))
-        ctx.capture = capture
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        grad_x = None
-        if ctx.capture and ctx.needs_input_grad[2]:
-            samples, takes = ctx.saved_tensors
-            grad_x = _backward_1hop(samples, takes, grad_out.contiguous(), ctx.num_nodes)
-        return None, None, grad_x, None, None, None, None, None
-
-
-class _FusedSampleAgg2HopFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, rowptr, col, x, frontier, fanout1, fanout2, replay_seed, save_indices,
-                batch_offset):
-        _check_python_inputs(rowptr, col, x, frontier)
-        capture = bool(save_indices) or x.requires_grad
-        # When the backward will need the dense feature gradient, allocate it
-        # now and let the forward's sampling kernel zero it: that kernel is
-        # bound by integer issue, the fill by HBM writes, so the fill costs
-        # little extra (the reference zero-fills inside the backward,
-        # fuseop/binding.cpp:220).
-        ctx.grad_buffer = None
-        if capture and ctx.needs_input_grad[2]:
-            ctx.grad_buffer = torch.empty((x.size(0), x.size(1)), dtype=torch.float32,
-                                          device=x.device)
-        out, s1, s2 = _forward_2hop(
-            rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
-            fanout1, fanout2, replay_seed, capture, batch_offset, zero=ctx.grad_buffer)
-        if capture:
-            ctx.save_for_backward(s1, s2)
-            ctx.num_nodes = int(x.size(0))
-        ctx.capture = capture
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        grad_x = None
-        if ctx.capture and ctx.needs_input_grad[2]:
-            s1, s2 = ctx.saved_tensors
-            grad_x = _backward_2hop(grad_out.contiguous(), s1, s2, ctx.num_nodes,
-                                    ctx.grad_buffer)
-        ctx.grad_buffer = None
-        return None, None, grad_x, None, None, None, None, None, None
-
-
-# ---------------------------------------------------------------------------
 # Public API (fuseop/__init__.py:75-206)
 # ---------------------------------------------------------------------------
 
 def fused_sample_agg(rowptr, col, x, frontier, fanout, replay_seed=1234, save_indices=False,
                      *, batch_offset=0):
     """Return the sampled 1-hop neighbor mean for each frontier node."""
-    return _FusedSampleAggFn.apply(rowptr, col, x, frontier, fanout, replay_seed, save_indices,
-                                   batch_offset)
+    _check_python_inputs(rowptr, col, x, frontier)
+    return _C.sample_agg(rowptr, col, x, frontier, _as_int64(fanout, "fanout"),
+                         _as_seed(replay_seed), bool(save_indices),
+                         _as_int64(batch_offset, "batch_offset"))
 
 
 def fused_sample_agg_with_samples(rowptr, col, x, frontier, fanout, replay_seed=1234,
@@ -391,17 +339,18 @@ def fused_sample_agg_with_samples(rowptr, col, x, frontier, fanout, replay_seed=
     no autograd.
     """
     _check_python_inputs(rowptr, col, x, frontier)
-    out, samples, takes = _forward_1hop(
-        rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
-        fanout, replay_seed, True, batch_offset)
-    return [out, samples, takes]
+    return _C.sample_agg_with_samples(rowptr, col, x, frontier, _as_int64(fanout, "fanout"),
+                                      _as_seed(replay_seed),
+                                      _as_int64(batch_offset, "batch_offset"))
 
 
 def fused_sample_agg_2hop(rowptr, col, x, frontier, fanout1, fanout2, replay_seed=1234,
                           save_indices=False, *, batch_offset=0):
     """Return the nested sampled 2-hop neighbor mean for each frontier node."""
-    return _FusedSampleAgg2HopFn.apply(rowptr, col, x, frontier, fanout1, fanout2, replay_seed,
-                                       save_indices, batch_offset)
+    _check_python_inputs(rowptr, col, x, frontier)
+    return _C.sample_agg_2hop(rowptr, col, x, frontier, _as_int64(fanout1, "fanout1"),
+                              _as_int64(fanout2, "fanout2"), _as_seed(replay_seed),
+                              bool(save_indices), _as_int64(batch_offset, "batch_offset"))
 
 
 def fused_sample_agg_2hop_with_samples(rowptr, col, x, frontier, fanout1, fanout2,
@@ -412,9 +361,10 @@ def fused_sample_agg_2hop_with_samples(rowptr, col, x, frontier, fanout1, fanout
     autograd.
     """
     _check_python_inputs(rowptr, col, x, frontier)
-    return _forward_2hop(
-        rowptr.contiguous(), col.contiguous(), x.contiguous(), frontier.contiguous(),
-        fanout1, fanout2, replay_seed, True, batch_offset)
+    return _C.sample_agg_2hop_with_samples(rowptr, col, x, frontier,
+                                           _as_int64(fanout1, "fanout1"),
+                                           _as_int64(fanout2, "fanout2"), _as_seed(replay_seed),
+                                           _as_int64(batch_offset, "batch_offset"))
 
 
 def launch_count() -> int:

@@ -165,3 +165,39 @@ def test_ipc_and_peer_helpers_reject_null_arguments():
     assert L.fsa_ipc_export(NULL, NULL, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
     assert L.fsa_ipc_open(NULL, 0, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
     assert L.fsa_ipc_close(NULL, 0) == _lib.FSA_ERR_INVALID_ARGUMENT
+
+
+# ---------------------------------------------------------------------------
+# The torch binding (_fsa_torch): loads without a GPU, links this library
+# ---------------------------------------------------------------------------
+
+def test_torch_binding_loads_and_exposes_the_operator():
+    from fusesampleagg_b200 import _fsa_torch
+
+    for name in ("sample_agg", "sample_agg_with_samples", "sample_agg_2hop",
+                 "sample_agg_2hop_with_samples"):
+        assert callable(getattr(_fsa_torch, name))
+
+
+def test_torch_binding_links_the_c_abi_library_from_its_own_directory():
+    import subprocess
+
+    from fusesampleagg_b200 import _fsa_torch
+
+    out = subprocess.run(["readelf", "-d", _fsa_torch.__file__], check=True,
+                         capture_output=True, text=True).stdout
+    assert "[libfsa_sm100.so]" in out
+    assert "$ORIGIN" in out
+
+
+def test_torch_binding_rejects_cpu_tensors_before_cuda():
+    import torch
+
+    from fusesampleagg_b200 import _fsa_torch
+
+    rp = torch.zeros(3, dtype=torch.int32)
+    x = torch.zeros(2, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _fsa_torch.sample_agg_2hop_with_samples(rp, rp, x, rp, 2, 2, 1, 0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _fsa_torch.sample_agg_with_samples(rp, rp, x, rp, 2, 1, 0)
