@@ -15,7 +15,12 @@ same neighbours.
 prints ``{"mean_step_ms": ..., "sampled_edges_per_second": ..., "steps": ...}``
 (plus ``"impl"``), where sampled edges = batch x fanout1 x fanout2 per step.
 ``--impl reference`` runs the reference op built from its sources into
-``oracle/_ref`` when that build exists.
+``oracle/_ref`` when that build exists.  ``--kernel-times`` (this package
+only) adds the per-kernel CUDA-event times of the forward and the gather
+kernel's algorithmic bandwidth: second-hop winner ids and their col entries
+(4 B each), the valid leaf rows (4·D B each) and the output (4·D B per
+root), against the measured HBM copy bandwidth in MEASURED_PEAKS.json when
+the repository holds one.
 """
 
 from __future__ import annotations
@@ -88,8 +93,50 @@ def run(args) -> dict:
     end.synchronize()
     ms = start.elapsed_time(end)
     edges = args.batch_size * f1 * f2 * args.steps
-    return {"impl": args.impl, "mean_step_ms": ms / args.steps,
-            "sampled_edges_per_second": edges / (ms / 1000.0), "steps": args.steps}
+    res = {"impl": args.impl, "mean_step_ms": ms / args.steps,
+           "sampled_edges_per_second": edges / (ms / 1000.0), "steps": args.steps}
+    if getattr(args, "kernel_times", False) and args.impl == "ours":
+        res["kernels"] = kernel_times(op, rowptr, col, x, roots, f1, f2, args)
+    return res
+
+
+def measured_hbm_gbs() -> tuple[float, str]:
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        return float(peaks["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+def kernel_times(op, rowptr, col, x, roots, f1, f2, args) -> dict:
+    """Per-kernel times of `args.steps` more forwards (the library's phase
+    events) and the gather kernel's algorithmic GB/s."""
+    from . import _lib
+
+    _lib.phase_timing(True)
+    try:
+        for step in range(args.steps):
+            op(rowptr, col, x, roots, f1, f2, args.seed + step)
+        torch.cuda.synchronize()
+        ms, calls = _lib.phase_times()
+    finally:
+        _lib.phase_timing(False)
+    us = {k: 1000.0 * v / calls for k, v in ms.items()}
+    # valid second-hop leaves of one call: every slot of a row whose take is
+    # positive holds a valid id (the ids come from the op itself)
+    from . import fused_sample_agg_2hop_with_samples
+
+    _, _, s2 = fused_sample_agg_2hop_with_samples(rowptr, col, x, roots, f1, f2, args.seed)
+    valid = int((s2 >= 0).sum())
+    B, D = roots.numel(), x.size(1)
+    gather_bytes = 4 * B * f1 * f2 + 4 * valid + 4 * D * valid + 4 * D * B
+    gbs = gather_bytes / (us["gather"] * 1e-6) / 1e9
+    peak, kind = measured_hbm_gbs()
+    return {"plan_us": us["plan"], "scan_us": us["scan"], "draw_us": us["draw"],
+            "gather_us": us["gather"],
+            "valid_leaves": valid, "gather_algorithmic_bytes": gather_bytes,
+            "gather_gbs": gbs, "peak_gbs": peak, "peak_kind": kind,
+            "gather_frac_of_peak": gbs / peak}
 
 
 def main(argv=None) -> None:
@@ -103,6 +150,8 @@ def main(argv=None) -> None:
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--kernel-times", action="store_true",
+                   help="add per-kernel times and the gather kernel's bandwidth (ours)")
     print(json.dumps(run(p.parse_args(argv)), sort_keys=True))
 
 

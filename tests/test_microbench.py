@@ -50,3 +50,17 @@ def test_microbench_run_fields():
     assert res["steps"] == 3 and res["mean_step_ms"] > 0
     assert res["sampled_edges_per_second"] == pytest.approx(
         256 * 150 * 3 / (res["mean_step_ms"] * 3 / 1000.0))
+
+
+@pytest.mark.gpu
+def test_microbench_kernel_times():
+    res = mb.run(type("A", (), dict(nodes=10_000, features=16, degree=20, batch_size=256,
+                                    fanout=[15, 10], steps=3, warmup=3, seed=1234,
+                                    impl="ours", kernel_times=True))())
+    k = res["kernels"]
+    # degree 20 >= both fanouts: every slot holds a valid leaf
+    assert k["valid_leaves"] == 256 * 150
+    assert k["gather_algorithmic_bytes"] == 4 * 256 * 150 * (1 + 1 + 16) + 4 * 16 * 256
+    for name in ("plan_us", "draw_us", "gather_us"):
+        assert k[name] > 0
+    assert k["gather_gbs"] > 0 and k["peak_gbs"] > 0
