@@ -397,3 +397,60 @@ def test_sorted_backward_on_c2_graph_matches_atomic_variant():
     got = sorted_backward(go, s1, s2, g.num_nodes)
     want = fsa._backward_2hop(go, s1, s2, g.num_nodes)
     torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
+
+
+# ---------------------------------------------------------------------------
+# Autograd behaviour of the C++ binding
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("hops", [1, 2])
+def test_non_contiguous_features_give_the_same_output_and_gradient(hops):
+    g = cpu_graph("powerlaw")
+    rp, cl = dev_graph("powerlaw")
+    base = cpu_features(g.num_nodes, 24).cuda()
+    fr = frontier("powerlaw", 64, 3).cuda()
+    go = synthetic.features(64, 24, seed=8).cuda()
+
+    def run(x):
+        if hops == 1:
+            return fsa.fused_sample_agg(rp, cl, x, fr, 10, replay_seed=4)
+        return fsa.fused_sample_agg_2hop(rp, cl, x, fr, 8, 4, replay_seed=4)
+
+    xa = base.clone().requires_grad_(True)
+    oa = run(xa)
+    oa.backward(go)
+    # same values, transposed storage: a non-contiguous leaf
+    xb = base.t().contiguous().t().requires_grad_(True)
+    assert not xb.is_contiguous()
+    ob = run(xb)
+    ob.backward(go)
+    assert torch.equal(oa.view(torch.int32), ob.view(torch.int32))
+    torch.testing.assert_close(xb.grad, xa.grad, rtol=RTOL, atol=ATOL)
+
+
+def test_no_grad_mode_records_no_graph_and_allocates_no_gradient():
+    rp, cl = dev_graph("powerlaw")
+    g = cpu_graph("powerlaw")
+    x = cpu_features(g.num_nodes, 16).cuda().requires_grad_(True)
+    fr = frontier("powerlaw", 32, 1).cuda()
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        before = torch.cuda.memory_allocated()
+        out = fsa.fused_sample_agg_2hop(rp, cl, x, fr, 8, 4, replay_seed=2)
+        torch.cuda.synchronize()
+        # ids for replay are captured (x.requires_grad), the dense N x D
+        # gradient buffer is not
+        assert torch.cuda.memory_allocated() - before < g.num_nodes * 16 * 4
+    assert out.grad_fn is None and not out.requires_grad
+
+
+def test_gradient_accumulates_over_two_backwards():
+    g = cpu_graph("hub")
+    rp, cl = dev_graph("hub")
+    x = cpu_features(g.num_nodes, 20).cuda().requires_grad_(True)
+    fr = frontier("hub", 48, 5).cuda()
+    go = synthetic.features(48, 20, seed=9).cuda()
+    fsa.fused_sample_agg_2hop(rp, cl, x, fr, 5, 10, replay_seed=6).backward(go)
+    once = x.grad.clone()
+    fsa.fused_sample_agg_2hop(rp, cl, x, fr, 5, 10, replay_seed=6).backward(go)
+    torch.testing.assert_close(x.grad, 2 * once, rtol=RTOL, atol=ATOL)
