@@ -369,6 +369,18 @@ __global__ void __launch_bounds__(kThreads1Hop)
 //   gather CTA per root: winners -> ids (col lookups), nested mean.
 // ---------------------------------------------------------------------------
 
+// Programmatic dependent launch (sm_90+).  The plan (or scan) kernel lets
+// the draw kernel launch while its own CTAs are still running; a thread of
+// the draw kernel that reads their results first waits for their grid to
+// complete and its memory to be visible.  Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 constexpr int kThreadsPlan = 128;
 constexpr int kThreadsScan = 1024;
 constexpr int kThreadsDraw = 768;
@@ -412,6 +424,9 @@ __global__ void __launch_bounds__(kThreadsPlan)
   const int nthreads = blockDim.x;
   const int64_t N = a.num_nodes;
   if (blockIdx.x == 0 && tid == 0) *a.next = 0;  // fill-block counter of the draw kernel
+  // The draw kernel may launch now: its fill needs nothing from this kernel,
+  // and its readers of this kernel's results wait for this grid first.
+  launch_dependents();
 
   for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
     const int32_t root = a.frontier[b];
@@ -480,22 +495,29 @@ struct Scan2Args {
 
 constexpr int kScanItems = 4;
 
-// Exclusive prefix of counts[0, n) into pre[0, n], pre[n] = total, by one
-// CTA of at most 1024 threads: tiles of blockDim * kScanItems entries; each
-// thread scans its contiguous items, warp shuffles and the warp totals give
-// the tile prefix, a running carry joins the tiles.  `warp_sums` ([32]) and
-// `carry` are shared scratch; pre may be global or shared memory.  All
-// threads of the CTA must call it.
-__device__ __forceinline__ void block_exclusive_scan(const long long* counts, long long* pre,
+// Barrier `id` among `nthreads` threads (whole warps) of the CTA; id 0 with
+// every thread of the CTA is __syncthreads.
+__device__ __forceinline__ void group_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Exclusive prefix of counts[0, n) into pre[0, n], pre[n] = total, by a
+// group of `nthreads` threads (whole warps, at most 1024; `tid` = index in
+// the group) meeting at barrier `bar`: tiles of nthreads * kScanItems
+// entries; each thread scans its contiguous items, warp shuffles and the
+// warp totals give the tile prefix, a running carry joins the tiles.
+// `warp_sums` ([32]) and `carry` are shared scratch; pre may be global or
+// shared memory.  Every thread of the group must call it.
+__device__ __forceinline__ void group_exclusive_scan(const long long* counts, long long* pre,
                                                      int64_t n, long long* warp_sums,
-                                                     long long* carry) {
-  const int tid = threadIdx.x;
+                                                     long long* carry, int tid, int nthreads,
+                                                     int bar) {
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int nw = blockDim.x >> 5;
+  const int nw = nthreads >> 5;
   if (tid == 0) *carry = 0;
-  __syncthreads();
-  const int64_t tile = static_cast<int64_t>(blockDim.x) * kScanItems;
+  group_sync(bar, nthreads);
+  const int64_t tile = static_cast<int64_t>(nthreads) * kScanItems;
   for (int64_t t0 = 0; t0 < n; t0 += tile) {
     const int64_t i0 = t0 + static_cast<int64_t>(tid) * kScanItems;
     long long v[kScanItems];
@@ -512,7 +534,7 @@ __device__ __forceinline__ void block_exclusive_scan(const long long* counts, lo
       if (lane >= o) incl += y;
     }
     if (lane == 31) warp_sums[warp] = incl;
-    __syncthreads();
+    group_sync(bar, nthreads);
     if (warp == 0) {
       long long w = lane < nw ? warp_sums[lane] : 0;
 #pragma unroll
@@ -522,19 +544,27 @@ __device__ __forceinline__ void block_exclusive_scan(const long long* counts, lo
       }
       if (lane < nw) warp_sums[lane] = w;
     }
-    __syncthreads();
+    group_sync(bar, nthreads);
     long long run = *carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - local;
 #pragma unroll
     for (int u = 0; u < kScanItems; ++u) {
       if (i0 + u < n) pre[i0 + u] = run;
       run += v[u];
     }
-    __syncthreads();
+    group_sync(bar, nthreads);
     if (tid == 0) *carry += warp_sums[nw - 1];
-    __syncthreads();
+    group_sync(bar, nthreads);
   }
   if (tid == 0) pre[n] = *carry;
-  __syncthreads();
+  group_sync(bar, nthreads);
+}
+
+// The same scan by every thread of the CTA.
+__device__ __forceinline__ void block_exclusive_scan(const long long* counts, long long* pre,
+                                                     int64_t n, long long* warp_sums,
+                                                     long long* carry) {
+  group_exclusive_scan(counts, pre, n, warp_sums, carry, static_cast<int>(threadIdx.x),
+                       static_cast<int>(blockDim.x), 0);
 }
 
 // Chunk prefix over the roots when it does not fit the draw kernel's shared
@@ -543,6 +573,7 @@ __device__ __forceinline__ void block_exclusive_scan(const long long* counts, lo
 __global__ void __launch_bounds__(kThreadsScan) fsa_2hop_scan_kernel(const Scan2Args a) {
   __shared__ long long warp_sums[32];
   __shared__ long long carry;
+  launch_dependents();  // the draw kernel's fill may start (see the plan kernel)
   block_exclusive_scan(a.counts, a.pre, a.n, warp_sums, &carry);
 }
 
@@ -593,19 +624,20 @@ __device__ __forceinline__ void fill_block(float4* fill, int64_t fill_vec4, long
   }
 }
 
-// Zeroes fill items claimed from *counter until none is left, by bulk copies
+// Zeroes fill items base + k for k = 0, 1, ... claimed from *counter
+// (shared or global memory) while base + k < end, by bulk copies
 // (evict-first in L2) from the zeroed shared block at shared-window address
 // `zero`.  One thread; returns after its copies have completed.
-__device__ __forceinline__ void fill_items_bulk(unsigned long long* counter, float4* fill,
+__device__ __forceinline__ void fill_items_bulk(unsigned long long* counter, long long base,
+                                                long long end, float4* fill,
                                                 int64_t fill_vec4, uint32_t zero) {
   constexpr int64_t kItem = 32LL * kFillItemVec4;
   constexpr int64_t kPiece = kZeroBytes / 16;
-  const long long nitems = (fill_vec4 + kItem - 1) / kItem;
   uint64_t policy = 0;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   bool issued = false;
-  for (long long item = static_cast<long long>(atomicAdd(counter, 1ULL)); item < nitems;
-       item = static_cast<long long>(atomicAdd(counter, 1ULL))) {
+  for (long long item = base + static_cast<long long>(atomicAdd(counter, 1ULL)); item < end;
+       item = base + static_cast<long long>(atomicAdd(counter, 1ULL))) {
     const int64_t v0 = item * kItem;
     const int64_t v1 = fill_vec4 - v0 < kItem ? fill_vec4 : v0 + kItem;
     for (int64_t v = v0; v < v1; v += kPiece) {
@@ -681,6 +713,13 @@ __device__ __forceinline__ void draw_chunk(const Draw2Args& a, const long long* 
               a.win2 + r * a.fanout2);
 }
 
+// Fill items zeroed from a CTA's own share before the plan kernel has
+// finished: kFillStaticNum / kFillStaticDen of all items, split evenly over
+// the CTAs; the rest are claimed from the global counter afterwards, which
+// balances CTAs that started late.
+constexpr int kFillStaticNum = 1;
+constexpr int kFillStaticDen = 2;
+
 // Persistent grid, two CTAs of 24 warps per SM.  Each CTA keeps a shared
 // copy of the one-chunk lane tables (64 KB, lane index innermost) and of
 // the root prefix.  Lane l of group G draws global chunk 32 G + l: two
@@ -689,17 +728,23 @@ __device__ __forceinline__ void draw_chunk(const Draw2Args& a, const long long* 
 // mostly share.
 //
 // Optionally the kernel also zeroes a buffer (the backward's dense
-// gradient) in 32 KB items claimed from the counter *next, which the plan
-// kernel resets.  The draw loop is bound by integer issue, the fill by HBM
-// writes, so they run side by side: warp 0 of each CTA drives the bulk-copy
-// engine (lane 0), warp 1 stores, the other warps draw.  (Warps that
-// alternated between the two would tie each one's progress to the
-// other's.)
+// gradient) in 32 KB items.  The draw loop is bound by integer issue, the
+// fill by HBM writes, so they run side by side: warp 0 of each CTA drives
+// the bulk-copy engine (lane 0), warp 1 stores, the other warps draw.
+// (Warps that alternated between the two would tie each one's progress to
+// the other's.)  The kernel is launched as a programmatic dependent of the
+// plan (or scan) kernel: the fill needs nothing from it, so the two fill
+// warps start on the CTA's static share of the items at once, and only
+// then wait for the plan's grid before claiming the remaining items from
+// the counter *next (reset by the plan kernel); the draw warps wait before
+// reading the plan's row table.
 __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Draw2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint64_t* s_k1 = reinterpret_cast<uint64_t*>(smem_raw);  // one-chunk lane tables, [p][nib][l]
   long long* s_rpre = reinterpret_cast<long long*>(smem_raw + kDrawTableBytes);  // [B + 1]
   float4* s_zero = reinterpret_cast<float4*>(smem_raw + kDrawTableBytes + kRprePad);
+  __shared__ unsigned long long s_fill_next;  // claims within the CTA's static share
+  launch_dependents();  // the gather kernel may launch; it waits for this grid
   const int lane = threadIdx.x & 31;
   const int64_t B = a.batch_size;
   const bool staged = B < a.smem_roots;
@@ -708,11 +753,7 @@ __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Dr
     uint4* dst = reinterpret_cast<uint4*>(s_k1);
     for (int t = threadIdx.x; t < kDrawTableBytes / 16; t += blockDim.x) dst[t] = __ldg(src + t);
   }
-  if (staged) {
-    // the chunk prefix over the roots, scanned by this CTA (no scan kernel)
-    __shared__ long long s_scan[33];
-    block_exclusive_scan(a.rgroups, s_rpre, B, s_scan, s_scan + 32);
-  }
+  if (threadIdx.x == 0) s_fill_next = 0;
   if (a.fill_vec4 > 0) {
     for (int t = threadIdx.x; t < kZeroBytes / 16; t += blockDim.x) {
       s_zero[t] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
@@ -721,27 +762,47 @@ __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Dr
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   __syncthreads();
-  const long long* rpre = staged ? s_rpre : a.rpre;
-  const long long total = rpre[B];
-  const long long nfill = (a.fill_vec4 + 32LL * kFillItemVec4 - 1) / (32LL * kFillItemVec4);
-  // Groups of 32 chunks cost about the same, so drawing warps take them
-  // round robin.
   const int warps = static_cast<int>(blockDim.x >> 5);
   const int warp = static_cast<int>(threadIdx.x >> 5);
-  const int fillers = nfill > 0 ? kFillWarps : 0;
-  if (warp == 0 && fillers > 0) {
-    if (lane == 0) {
-      fill_items_bulk(a.next, a.fill, a.fill_vec4,
-                      static_cast<uint32_t>(__cvta_generic_to_shared(s_zero)));
-    }
-    return;
-  }
+  const int fillers = a.fill_vec4 > 0 ? kFillWarps : 0;
   if (warp < fillers) {
-    for (long long item = claim(a.next, lane); item < nfill; item = claim(a.next, lane)) {
+    const long long nfill = (a.fill_vec4 + 32LL * kFillItemVec4 - 1) / (32LL * kFillItemVec4);
+    const long long share = nfill * kFillStaticNum / kFillStaticDen / gridDim.x;
+    const long long share0 = static_cast<long long>(blockIdx.x) * share;
+    const long long dyn0 = static_cast<long long>(gridDim.x) * share;
+    if (warp == 0) {
+      if (lane == 0) {
+        const uint32_t zero = static_cast<uint32_t>(__cvta_generic_to_shared(s_zero));
+        fill_items_bulk(&s_fill_next, share0, share0 + share, a.fill, a.fill_vec4, zero);
+        wait_prerequisites();
+        fill_items_bulk(a.next, dyn0, nfill, a.fill, a.fill_vec4, zero);
+      }
+      return;
+    }
+    for (long long item = share0 + claim(&s_fill_next, lane); item < share0 + share;
+         item = share0 + claim(&s_fill_next, lane)) {
+      fill_block(a.fill, a.fill_vec4, item, lane);
+    }
+    wait_prerequisites();
+    for (long long item = dyn0 + claim(a.next, lane); item < nfill;
+         item = dyn0 + claim(a.next, lane)) {
       fill_block(a.fill, a.fill_vec4, item, lane);
     }
     return;
   }
+  wait_prerequisites();
+  if (staged) {
+    // the chunk prefix over the roots, scanned by this CTA's drawing warps
+    // (no scan kernel)
+    __shared__ long long s_scan[33];
+    group_exclusive_scan(a.rgroups, s_rpre, B, s_scan, s_scan + 32,
+                         static_cast<int>(threadIdx.x) - 32 * fillers, 32 * (warps - fillers),
+                         1);
+  }
+  const long long* rpre = staged ? s_rpre : a.rpre;
+  const long long total = rpre[B];
+  // Groups of 32 chunks cost about the same, so drawing warps take them
+  // round robin.
   const long long ngroups = (total + 31) / 32;
   const long long stride = static_cast<long long>(gridDim.x) * (warps - fillers);
   for (long long G = static_cast<long long>(blockIdx.x) * (warps - fillers) + (warp - fillers);
@@ -826,6 +887,10 @@ __global__ void __launch_bounds__(kThreadsGather, 4)
   const int k12 = k1 * k2;
   const int64_t D = a.feature_dim;
   const int64_t N = a.num_nodes;
+  // Launched as a programmatic dependent of the draw kernel: everything
+  // below reads its results.  The backward may launch behind this kernel.
+  wait_prerequisites();
+  launch_dependents();
 
   for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
     // Winners -> second-hop ids: slot j of a row holds col[winner], or
@@ -985,6 +1050,9 @@ __global__ void __launch_bounds__(kThreadsBwd)
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
   const int64_t dvec = a.feature_dim / V;
+  // May be launched as a programmatic dependent of the kernel before it:
+  // wait for that grid before reading anything.
+  wait_prerequisites();
 
   for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
     if (tid == 0) misc[0] = 0;
@@ -1259,6 +1327,34 @@ int launch(Kernel kernel, int grid, int block, int smem, cudaStream_t stream,
   return check_launch();
 }
 
+// The same launch as a programmatic dependent of the kernel before it in
+// the stream (cudaLaunchAttributeProgrammaticStreamSerialization): it may
+// start once every CTA of that kernel has run griddepcontrol.launch_dependents,
+// and must itself wait (griddepcontrol.wait) before reading that kernel's
+// results.
+template <class Kernel, class Args>
+int launch_dependent(Kernel kernel, int grid, int block, int smem, cudaStream_t stream,
+                     const Args& args) {
+  if (smem > 48 * 1024) {
+    const cudaError_t err =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return cuda_fail(err);
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned int>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned int>(block));
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args);
+  if (err != cudaSuccess) return cuda_fail(err);
+  return check_launch();
+}
+
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 // Optional per-kernel timing of the 2-hop forward (fsa_phase_timing): five
@@ -1523,7 +1619,7 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
   const Draw2Args da{rgroups, rpre, lpre, state, mtake, mdraws, batch_size, fanout1, fanout2,
                      win2, next, fill4, fill_vec4, kSmemRoots};
   const int dsmem = kDrawTableBytes + kRprePad + (fill_vec4 > 0 ? kZeroBytes : 0);
-  st = launch(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
+  st = launch_dependent(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st == FSA_OK) st = pe.mark(3, s);
   if (st != FSA_OK) return st;
   Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
@@ -1538,9 +1634,9 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
     }
   } else {
     switch (vec) {
-      case 4: st = launch(fsa_2hop_gather_kernel<4, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
-      case 2: st = launch(fsa_2hop_gather_kernel<2, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
-      default: st = launch(fsa_2hop_gather_kernel<1, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
+      case 4: st = launch_dependent(fsa_2hop_gather_kernel<4, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
+      case 2: st = launch_dependent(fsa_2hop_gather_kernel<2, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
+      default: st = launch_dependent(fsa_2hop_gather_kernel<1, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
     }
   }
   if (st == FSA_OK) st = pe.mark(4, s);
@@ -1635,9 +1731,9 @@ static int backward_2hop(const float* grad_out, const int32_t* samples1,
     }
   }
   switch (vec) {
-    case 4: return launch(fsa_2hop_backward_kernel<4, false>, grid, kThreadsBwd, smem, s, a);
-    case 2: return launch(fsa_2hop_backward_kernel<2, false>, grid, kThreadsBwd, smem, s, a);
-    default: return launch(fsa_2hop_backward_kernel<1, false>, grid, kThreadsBwd, smem, s, a);
+    case 4: return launch_dependent(fsa_2hop_backward_kernel<4, false>, grid, kThreadsBwd, smem, s, a);
+    case 2: return launch_dependent(fsa_2hop_backward_kernel<2, false>, grid, kThreadsBwd, smem, s, a);
+    default: return launch_dependent(fsa_2hop_backward_kernel<1, false>, grid, kThreadsBwd, smem, s, a);
   }
 }
 
