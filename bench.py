@@ -310,11 +310,14 @@ def make_step(api, w, inp: Inputs, batch_offset: bool):
 def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
     """Public-API step with host buffers: every step copies its roots and
     upstream gradient from pinned host memory (one packed buffer per root
-    batch, one copy) and reads its output back into pinned memory.  As a
-    data loader would, the copies run on a second stream: step i+1's inputs
-    are copied while step i computes (double buffered), and step i's output
-    is read back while step i+1 computes.  `reset()` drops the prefetched
-    inputs, so the first step after it copies its own inputs first."""
+    batch, one copy) and reads its output back into pinned memory, where the
+    host reads it.  As a data loader would, the copies run on a second
+    stream: step i+1's inputs are copied while step i computes (double
+    buffered), and step i's output is read back while step i+1 computes; the
+    host reads step i's output at the start of step i+2 (waiting for its
+    copy), which also bounds how far the host runs ahead of the GPU.
+    `reset()` drops the prefetched inputs, so the first step after it copies
+    its own inputs first."""
     k1, k2 = w.fanouts
     nb = len(inp.frontiers)
     kw = {"batch_offset": inp.offset} if batch_offset else {}
@@ -341,6 +344,7 @@ def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
     for h in host_out:
         h.copy_(dev_in[0][: h.numel() * 4].view(torch.float32).view_as(h), non_blocking=True)
     torch.cuda.synchronize(dev)
+    comp = torch.cuda.current_stream(dev)
     copy = torch.cuda.Stream(device=dev)
     free = [None, None]       # event after the last compute that read a slot
     ready = {}                # step -> event of its input copy
@@ -349,6 +353,9 @@ def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
     # record has been enqueued (a wait binds to the record it sees).
     ready_ev = [torch.cuda.Event() for _ in range(2)]
     done_ev = [torch.cuda.Event() for _ in range(2)]
+    out_ev = [torch.cuda.Event() for _ in range(2)]
+    pending = [False, False]  # an output copy into host_out[slot] not read yet
+    checksum = [0.0]
 
     def copy_inputs(i):
         # on the copy stream
@@ -361,11 +368,16 @@ def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
         ready[i] = ev
 
     def step(i):
-        comp = torch.cuda.current_stream()
         slot = i % 2
+        if pending[slot]:
+            # the host reads step i-2's result before its buffer is reused
+            out_ev[slot].synchronize()
+            checksum[0] += float(host_out[slot][0, 0])
+            pending[slot] = False
         if i not in ready:
-            with torch.cuda.stream(copy):
-                copy_inputs(i)
+            torch.cuda.set_stream(copy)
+            copy_inputs(i)
+            torch.cuda.set_stream(comp)
         comp.wait_event(ready.pop(i))
         inp.x.grad = None
         out = api.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, dev_fr[slot], k1, k2,
@@ -374,15 +386,18 @@ def make_e2e_step(api, w, inp: Inputs, batch_offset: bool):
         done = done_ev[slot]
         done.record(comp)
         free[slot] = done
-        with torch.cuda.stream(copy):
-            copy_inputs(i + 1)          # does not wait for this step's compute
-            copy.wait_event(done)
-            host_out[slot].copy_(out.detach(), non_blocking=True)
+        torch.cuda.set_stream(copy)
+        copy_inputs(i + 1)              # does not wait for this step's compute
+        copy.wait_event(done)
+        host_out[slot].copy_(out.detach(), non_blocking=True)
+        out_ev[slot].record(copy)
+        torch.cuda.set_stream(comp)
+        pending[slot] = True
         out.record_stream(copy)
 
     step.reset = ready.clear
     # the last output read-back belongs to the timed region
-    step.drain = lambda: torch.cuda.current_stream().wait_stream(copy)
+    step.drain = lambda: comp.wait_stream(copy)
     return step, nbytes, d2h
 
 
@@ -714,7 +729,8 @@ def run(args) -> None:
                 "copies": "roots + upstream gradient packed in one pinned buffer per root "
                           "batch, one H2D per step issued one step ahead on a copy stream "
                           "(double-buffered), output D2H into pinned memory overlapping the "
-                          "next step; the first timed step copies its own inputs"},
+                          "next step and read by the host two steps later; the first timed "
+                          "step copies its own inputs"},
         "clocks": clocks,
     }
     if args.allreduce_grad:

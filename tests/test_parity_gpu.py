@@ -454,3 +454,32 @@ def test_gradient_accumulates_over_two_backwards():
     once = x.grad.clone()
     fsa.fused_sample_agg_2hop(rp, cl, x, fr, 5, 10, replay_seed=6).backward(go)
     torch.testing.assert_close(x.grad, 2 * once, rtol=RTOL, atol=ATOL)
+
+
+# ---------------------------------------------------------------------------
+# Fanouts at the shared-memory limit (f1 + f1 * f2 <= 12000)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("fan", [(5, 2399), (1, 11999), (109, 109)])
+def test_2hop_at_the_entry_limit_matches_oracle(fan):
+    # hub graph: root 9 links to rows 0 (60,000 neighbours), 8 (20,000), 6
+    # and 7 (1024 / 1025), so second-hop rows draw far past the fanout
+    k1, k2 = fan
+    assert k1 + k1 * k2 <= 12000
+    g = cpu_graph("hub")
+    out, s1, s2, ref_out, r1, r2 = run_2hop("hub", k1, k2, 3, dim=8, batch=16)
+    np.testing.assert_array_equal(s1.cpu().numpy(), r1)
+    np.testing.assert_array_equal(s2.cpu().numpy(), r2)
+    assert_bit_equal(out, ref_out)
+    go = synthetic.features(16, 8, seed=4)
+    grad = fsa._backward_2hop(go.cuda(), s1, s2, g.num_nodes)
+    ref = oracle.backward_2hop(go.numpy(), r1, r2, g.num_nodes)
+    np.testing.assert_allclose(grad.cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
+
+
+def test_2hop_just_over_the_entry_limit_is_rejected():
+    rp, cl = dev_graph("hub")
+    x = cpu_features(70_000, 8).cuda()
+    fr = frontier("hub", 16, 3).cuda()
+    with pytest.raises(RuntimeError, match="shared memory"):
+        fsa.fused_sample_agg_2hop(rp, cl, x, fr, 5, 2400)
