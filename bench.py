@@ -57,15 +57,15 @@ NOMINAL_HBM_GBS = 8000.0
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum, in
 # bytes) that ncu measured for each kernel of a workload, from the captures
 # summarised in profiles/ (commands there).  The draw kernel with the fused
-# fill writes 918 MB of the 980 MB fill during its own launch; the rest
+# fill writes 919 MB of the 980 MB fill during its own launch; the rest
 # leaves L2 as dirty lines during the next kernels.
 NCU_TRAFFIC = {
     "c2_2hop_powerlaw": {
-        "draw": 1.03e6 + 918.0e6,
-        "gather": 55.6e6 + 0.02e6,
-        "plan": 1.87e6,
+        "draw": 1.09e6 + 919.0e6,
+        "gather": 56.0e6 + 0.05e6,
+        "plan": 1.86e6,
         "scan": 0.02e6,
-        "bwd": 42.5e6 + 2.2e6,
+        "bwd": 42.65e6 + 2.38e6,
     },
 }
 
