@@ -19,7 +19,12 @@
  * row-major, frontier int32[batch_size].  All pointers are device pointers.
  * Calls are asynchronous and stream-ordered; nothing is allocated (scratch
  * comes from a caller-provided workspace where a call needs one) and the
- * host is never synchronised (except fsa_device_status).
+ * host is never synchronised (except fsa_device_status).  The 2-hop draw,
+ * gather and backward kernels are launched as programmatic dependents
+ * (cudaLaunchAttributeProgrammaticStreamSerialization) of the kernel before
+ * them in the stream: they may be scheduled while it finishes, and every
+ * read of earlier work waits for it (griddepcontrol.wait), so the stream
+ * order a caller sees is unchanged.
  */
 #ifndef FSA_SM100_H_
 #define FSA_SM100_H_
