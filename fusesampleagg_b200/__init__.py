@@ -171,32 +171,10 @@ def _grad_buffer(zeroed, num_nodes, dim, device, stream) -> torch.Tensor:
 
 
 # ---------------------------------------------------------------------------
-# Launch wrappers (the binding layer, fuseop/binding.cpp:74-231)
+# Backward launch wrappers over ctypes (fuseop/binding.cpp:119-145, :200-231):
+# the public functions' autograd runs in the C++ binding; these serve direct
+# replays of saved ids.
 # ---------------------------------------------------------------------------
-
-def _forward_1hop(rowptr, col, x, frontier, fanout, seed, capture, batch_offset=0):
-    _check_graph_inputs(rowptr, col, x, frontier)
-    fanout = _as_int64(fanout, "fanout")
-    _check_fanout_1hop(fanout)
-    seed = _as_seed(seed)
-    off = _check_offset(batch_offset)
-    B, D = frontier.size(0), x.size(1)
-    with _DeviceGuard(x.device):
-        if B == 0 or fanout == 0:
-            out = torch.zeros((B, D), dtype=x.dtype, device=x.device)
-            samples = torch.full((B, fanout), -1, dtype=torch.int32, device=x.device)
-            takes = torch.zeros((B,), dtype=torch.int32, device=x.device)
-            return out, samples, takes
-        out = torch.empty((B, D), dtype=x.dtype, device=x.device)
-        samples = torch.empty((B, fanout), dtype=torch.int32, device=x.device) if capture else None
-        takes = torch.empty((B,), dtype=torch.int32, device=x.device) if capture else None
-        status = _L.fsa_sample_agg_forward(
-            rowptr.data_ptr(), col.data_ptr(), x.size(0), col.numel(), x.data_ptr(), D,
-            frontier.data_ptr(), B, off, fanout, seed, out.data_ptr(), _ptr(samples),
-            _ptr(takes), _stream_handle(x.device))
-        _lib.check(status, "fsa_sample_agg_forward")
-    return out, samples, takes
-
 
 def _backward_1hop(samples, takes, grad_out, num_nodes):
     if not (samples.is_cuda and takes.is_cuda and grad_out.is_cuda):
@@ -226,65 +204,6 @@ def _backward_1hop(samples, takes, grad_out, num_nodes):
             grad_x.data_ptr(), num_nodes, stream)
         _lib.check(status, "fsa_sample_agg_backward")
     return grad_x
-
-
-_ws_sizes: dict = {}
-
-
-def _workspace_bytes_2hop(B: int, fanout1: int, fanout2: int, capture: bool) -> int:
-    key = (B, fanout1, fanout2, capture)
-    n = _ws_sizes.get(key)
-    if n is None:
-        if len(_ws_sizes) >= 1024:
-            _ws_sizes.clear()
-        n = _ws_sizes[key] = _L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2,
-                                                                   int(capture), int(capture))
-    return n
-
-
-def _forward_2hop(rowptr, col, x, frontier, fanout1, fanout2, seed, capture, batch_offset=0,
-                  zero=None):
-    _check_graph_inputs(rowptr, col, x, frontier)
-    fanout1 = _as_int64(fanout1, "fanout1")
-    fanout2 = _as_int64(fanout2, "fanout2")
-    _check_fanout_2hop(fanout1, fanout2)
-    seed = _as_seed(seed)
-    off = _check_offset(batch_offset)
-    B, D = frontier.size(0), x.size(1)
-    dev = x.device
-    with _DeviceGuard(dev):
-        if B == 0 or fanout1 == 0 or fanout2 == 0:
-            out = torch.zeros((B, D), dtype=x.dtype, device=dev)
-            s1 = torch.full((B, fanout1), -1, dtype=torch.int32, device=dev)
-            s2 = torch.full((B, fanout1, fanout2), -1, dtype=torch.int32, device=dev)
-            if zero is not None:
-                zero.zero_()
-            return out, s1, s2
-        out = torch.empty((B, D), dtype=x.dtype, device=dev)
-        ws_bytes = _workspace_bytes_2hop(B, fanout1, fanout2, capture)
-        if capture:
-            # samples1, samples2 and the workspace share one allocation, each
-            # part starting on a 256-byte boundary
-            n1 = B * fanout1
-            n2 = n1 * fanout2
-            o2 = (n1 + 63) // 64 * 64
-            ow = (o2 + n2 + 63) // 64 * 64
-            buf = torch.empty((ow + (ws_bytes + 3) // 4,), dtype=torch.int32, device=dev)
-            s1 = buf[:n1].view(B, fanout1)
-            s2 = buf[o2:o2 + n2].view(B, fanout1, fanout2)
-            ws_ptr = buf.data_ptr() + 4 * ow
-        else:
-            s1 = s2 = None
-            ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
-            ws_ptr = ws.data_ptr()
-        zero_ptr = zero.data_ptr() if zero is not None else None
-        zero_count = zero.numel() if zero is not None else 0
-        status = _L.fsa_sample_agg_2hop_forward(
-            rowptr.data_ptr(), col.data_ptr(), x.size(0), col.numel(), x.data_ptr(), D,
-            frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(), _ptr(s1),
-            _ptr(s2), ws_ptr, ws_bytes, zero_ptr, zero_count, _stream_handle(dev))
-        _lib.check(status, "fsa_sample_agg_2hop_forward")
-    return out, s1, s2
 
 
 def _backward_2hop(grad_out, samples1, samples2, num_nodes, zeroed=None):
