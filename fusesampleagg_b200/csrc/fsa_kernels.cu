@@ -24,10 +24,16 @@
 //     0.0f, / valid; slot means in i order, / non-empty (IEEE division), so
 //     forward outputs are bit-identical.  Rows are read with
 //     ld.global.nc.L1::no_allocate.v{4,2,1}.f32 by feature width.
-//   * Backward: red.global.add.v{4,2}.f32 of (grad/nonempty)/valid.
-//   * No kernel allocates, synchronises with the host or waits on another
-//     thread block.  Out-of-range ids are never dereferenced: they are skipped
-//     and reported in a per-device status word.
+//   * Backward: red.global.add.v{4,2}.f32 of (grad/nonempty)/valid; a
+//     sort-by-destination variant (one store per touched row) is kept as a
+//     measured alternative.
+//   * Draw, gather and backward are programmatic dependent launches: they
+//     may start while the kernel before them finishes, and wait for it
+//     (griddepcontrol.wait) before reading its results -- so the gradient
+//     fill, which needs nothing from the plan kernel, starts early.
+//   * No kernel allocates, synchronises with the host or spins on another
+//     thread block.  Out-of-range ids are never dereferenced: they are
+//     skipped and reported in a per-device status word.
 #include <cuda_runtime.h>
 
 #include <array>
