@@ -47,7 +47,19 @@ import torch
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-from fusesampleagg_b200 import synthetic  # noqa: E402
+
+def _load_by_path(name: str, path: Path):
+    """Imports one module file without importing the package around it:
+    `fusesampleagg_b200/__init__.py` loads the library's .so files, which the
+    reference arm must not map."""
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod  # dataclasses look their module up while it executes
+    spec.loader.exec_module(mod)
+    return mod
+
+
+synthetic = _load_by_path("_fsa_bench_synthetic", REPO / "fusesampleagg_b200" / "synthetic.py")
 
 METRIC = "2-hop fwd+bwd roots/s"
 PEAKS_PATH = REPO / "MEASURED_PEAKS.json"
@@ -611,6 +623,162 @@ def sharded_api(inp: Inputs, w):
     return Api, feats
 
 
+def mapped_repo_libraries() -> list[str]:
+    """Shared objects under this repository mapped into this process
+    (/proc/self/maps), as paths relative to the repository."""
+    found = set()
+    try:
+        with open("/proc/self/maps") as fh:
+            for line in fh:
+                parts = line.split()
+                if len(parts) >= 6 and ".so" in parts[-1]:
+                    p = Path(parts[-1])
+                    if p.is_relative_to(REPO):
+                        found.add(str(p.relative_to(REPO)))
+    except OSError:
+        pass
+    return sorted(found)
+
+
+def check_reference_arm_libraries() -> list[str]:
+    """The reference arm may map the reference op's own extension and nothing
+    else built in this repository."""
+    libs = mapped_repo_libraries()
+    foreign = [p for p in libs if not p.startswith("oracle/_ref/fuseop/")]
+    if foreign:
+        raise SystemExit(f"reference arm mapped this repository's libraries: {foreign}")
+    return libs
+
+
+def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
+    """The row-sharded mode on the same global batch (2+ GPUs): this rank's
+    ids and outputs against the replicated op's for the same slice, bit for
+    bit; its gradient shard against the rows it owns of the all-reduced
+    replicated gradient (rtol 1e-5 / atol 1e-6); then the same timed step
+    through the sharded API.  Every rank takes the same collective steps."""
+    import torch.distributed as tdist
+
+    import fusesampleagg_b200 as fsa
+    from fusesampleagg_b200 import sharding
+
+    k1, k2 = w.fanouts
+    start, stop = sharding.shard_span(inp.n, dist.rank, dist.world)
+    feats = sharding.ShardedFeatures(inp.x.detach()[start:stop].clone().requires_grad_(True),
+                                     inp.n)
+    exact = True
+    checked = min(4, len(inp.frontiers))
+    with torch.no_grad():
+        for j in range(checked):
+            ro, r1, r2 = fsa.fused_sample_agg_2hop_with_samples(
+                inp.rowptr, inp.col, inp.x.detach(), inp.frontiers[j], k1, k2,
+                replay_seed=inp.seeds[j], batch_offset=inp.offset)
+            so, q1, q2 = sharding._forward_2hop_sharded(
+                inp.rowptr, inp.col, feats, inp.frontiers[j], k1, k2, inp.seeds[j], True,
+                inp.offset, None)
+            exact &= (torch.equal(ro.view(torch.int32), so.view(torch.int32))
+                      and torch.equal(r1, q1) and torch.equal(r2, q2))
+    # gradients: replicated per-rank gradient summed over the ranks vs shards
+    inp.x.grad = None
+    fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, inp.frontiers[0], k1, k2,
+                              replay_seed=inp.seeds[0], batch_offset=inp.offset
+                              ).backward(inp.grad_out)
+    full = inp.x.grad
+    inp.x.grad = None
+    tdist.all_reduce(full)
+    sharding.fused_sample_agg_2hop_sharded(inp.rowptr, inp.col, feats, inp.frontiers[0], k1, k2,
+                                           inp.seeds[0], inp.offset).backward(inp.grad_out)
+    torch.cuda.synchronize()
+    err = (feats.grad - full[start:stop]).abs()
+    tol = 1e-6 + 1e-5 * full[start:stop].abs()
+    grad_ok = bool((err <= tol).all())
+    max_err = float(err.max()) if err.numel() else 0.0
+    del full, err, tol
+    torch.cuda.empty_cache()
+    flags = torch.tensor([float(exact), float(grad_ok)], device="cuda")
+    tdist.all_reduce(flags, op=tdist.ReduceOp.MIN)
+
+    class Api:
+        @staticmethod
+        def fused_sample_agg_2hop(rowptr, col, x, frontier, f1, f2, replay_seed=1234,
+                                  batch_offset=0):
+            return sharding.fused_sample_agg_2hop_sharded(rowptr, col, feats, frontier, f1, f2,
+                                                          replay_seed, batch_offset)
+
+    launches0 = fsa.launch_count()
+    ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
+    launches = (fsa.launch_count() - launches0) * args.steps // (args.steps + args.warmup)
+    feats.close()
+    del feats
+    torch.cuda.empty_cache()
+    units = w.batch * dist.world * args.steps
+    return {
+        "value": units / (ms / 1000.0),
+        "unit": "roots/s",
+        "ms_per_step": ms / args.steps,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "bit_exact": bool(flags[0].item() == 1.0),
+        "bit_exact_checked": (f"ids (samples1, samples2) and outputs of {checked} root batches "
+                              "on every rank against the replicated op on the same slice"),
+        "grad_within_tol": bool(flags[1].item() == 1.0),
+        "grad_check": ("each rank's gradient shard vs its rows of the NCCL-all-reduced "
+                       "replicated gradient, rtol 1e-5 / atol 1e-6"),
+        "grad_max_abs_err_rank0": max_err,
+        "gpu_launches": launches,
+        "mode": ("feature rows and their gradient block-sharded over the GPUs: remote rows "
+                 "read and gradient added over NVLink through peer pointers (plain loads and "
+                 "red.add, no multicast); one-float NCCL all-reduce after forward and "
+                 "backward as the cross-GPU ordering"),
+    }
+
+
+def c5_leg(args, dist: Dist, dev) -> dict:
+    """The 100M-node scaling configuration (2-hop (15, 10), 1.6B directed
+    edges, D = 128, 65,536 roots per GPU): features replicated on one GPU,
+    row-sharded over the GPUs (gradient owner-sharded: every rank's
+    contributions are added into the owning rank's rows over NVLink) on 2 or
+    more.  Device-timed like the main measurement, max over ranks."""
+    import fusesampleagg_b200 as api
+    from fusesampleagg_b200 import sharding
+
+    w5 = synthetic.WORKLOADS["c5_2hop_100m"]
+    t0 = time.time()
+    inp = Inputs(w5, dev, dist.rank, dist.world, batches=4)
+    setup_s = time.time() - t0
+    log(f"[rank {dist.rank}] c5 setup {setup_s:.1f}s graph {inp.stats}")
+    feats = None
+    step_api = api
+    if dist.world >= 2:
+        step_api, feats = sharded_api(inp, w5)
+    steps, warmup = min(args.steps, 20), 3
+    sampler = ClockSampler(dist.local_rank) if dist.rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms, _ = timed(make_step(step_api, w5, inp, batch_offset=True), steps, warmup, dist, sampler)
+    clocks = sampler.stop() if sampler else None
+    if feats is not None:
+        feats.close()
+    units = w5.batch * dist.world * steps
+    out = {
+        "value": units / (ms / 1000.0),
+        "unit": "roots/s",
+        "ms_per_step": ms / steps,
+        "steps": steps,
+        "warmup": warmup,
+        "config": {**w5.describe(), "realized_edges": inp.stats["num_edges"],
+                   "realized_max_degree": inp.stats["max_degree"],
+                   "roots_per_gpu": w5.batch, "global_batch": w5.batch * dist.world},
+        "mode": ("replicated features on one GPU" if feats is None else
+                 f"row-sharded features over {dist.world} GPUs (gradient owner-sharded over "
+                 "NVLink)"),
+        "setup_s": round(setup_s, 1),
+        "clocks": clocks,
+    }
+    del inp, feats
+    torch.cuda.empty_cache()
+    return out
+
+
 def load_reference_op():
     ref_dir = REPO / "oracle" / "_ref" / "fuseop"
     if not (ref_dir / "__init__.py").exists():
@@ -682,7 +850,10 @@ def run(args) -> None:
     e2e_value = units / (e2e_ms / 1000.0)
     used = sorted({(args.warmup + i) % batches for i in range(args.steps)})
     torch.cuda.empty_cache()  # the steps' cached gradient buffers (51 GB each on C5)
-    bytes_model = byte_model(w, inp, used[: min(len(used), 16)]) if feats is None else None
+    # (this package's own samples: our arm only -- the reference arm maps none
+    # of this repository's libraries)
+    bytes_model = (byte_model(w, inp, used[: min(len(used), 16)])
+                   if feats is None and args.impl == "ours" else None)
     peak, peak_kind = load_peaks()
     if feats is not None:
         feats.close()
@@ -813,6 +984,18 @@ def run(args) -> None:
                                "fuseop/binding.cpp built for sm_100 from its sources) through "
                                "its public Python API")
         result["cpu_baseline"] = None
+        # Only the reference's extension may be mapped in this arm (checked
+        # after every step has run).
+        result["repo_libraries_mapped"] = check_reference_arm_libraries()
+    if args.impl == "ours" and feats is None and not args.allreduce_grad:
+        if world >= 2 and not args.no_sharded_leg:
+            result["sharded"] = sharded_leg(w, inp, args, dist)
+        if not args.no_c5 and args.workload != "c5_2hop_100m":
+            # C2's graph, features and step buffers go before C5 is built
+            del step, e2e_step, inp
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            result["c5"] = c5_leg(args, dist, dev)
     dist.close()
     if dist.rank == 0:
         emit(result)
@@ -883,6 +1066,11 @@ def main() -> None:
     p.add_argument("--cpu-budget", type=float, default=12.0)
     p.add_argument("--sharded", action="store_true",
                    help="row-shard the features over the ranks (peer reads over NVLink)")
+    p.add_argument("--no-sharded-leg", action="store_true",
+                   help="on 2+ GPUs, skip the row-sharded check and timing after the main "
+                        "measurement")
+    p.add_argument("--no-c5", action="store_true",
+                   help="skip the 100M-node configuration after the main measurement")
     p.add_argument("--allreduce-grad", action="store_true",
                    help="replicated features: all-reduce the dense feature gradient after "
                         "every backward (NCCL)")

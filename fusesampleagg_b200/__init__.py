@@ -13,10 +13,14 @@ Sampled neighbour ids are bit-identical to the reference for the same
 as well (same fp32 summation order); feature gradients match to fp32
 rounding (atomic accumulation order differs, as in the reference).
 
-One addition over the reference API: a keyword-only ``batch_offset``
-(default 0) that is added to the batch index in the first-hop seeds, so a
-contiguous slice of a larger batch -- e.g. one GPU's share of the roots --
-draws exactly the samples the whole batch would.
+Two additions over the reference API, both keyword-only:
+
+* ``batch_offset`` (default 0) is added to the batch index in the first-hop
+  seeds, so a contiguous slice of a larger batch -- e.g. one GPU's share of
+  the roots -- draws exactly the samples the whole batch would;
+* ``grad_buffer`` (default None) takes a ``PersistentGradient``: the
+  backward adds into that buffer instead of returning a fresh dense N x D
+  gradient, and the buffer is cleared row by row (see PersistentGradient).
 """
 
 from __future__ import annotations
@@ -46,7 +50,11 @@ _I64_MAX = (1 << 63) - 1
 
 
 # ---------------------------------------------------------------------------
-# Argument checks (fuseop/__init__.py:15-29 and fuseop/binding.cpp:16-53)
+# Argument checks.  The Python-side ValueError / TypeError checks of
+# fuseop/__init__.py:15-29 run here; the RuntimeError checks of
+# fuseop/binding.cpp:16-53, :119-135 and :200-218 run in the C++ binding
+# (csrc/fsa_torch.cpp).  The row-sharded entry (sharding.py), which calls the
+# C ABI directly, uses the integer, fanout and offset checks below.
 # ---------------------------------------------------------------------------
 
 def _check_python_inputs(rowptr, col, x, frontier) -> None:
@@ -58,26 +66,6 @@ def _check_python_inputs(rowptr, col, x, frontier) -> None:
         raise TypeError("frontier must have dtype torch.int32")
     if x.dtype != torch.float32:
         raise TypeError("x must have dtype torch.float32")
-
-
-def _check_graph_inputs(rowptr, col, x, frontier) -> None:
-    dev = x.device
-    if not (x.is_cuda and rowptr.is_cuda and col.is_cuda and frontier.is_cuda):
-        raise RuntimeError("all inputs must be CUDA tensors")
-    if rowptr.device != dev or col.device != dev or frontier.device != dev:
-        raise RuntimeError("all inputs must be on the same CUDA device")
-    i32 = torch.int32
-    if rowptr.dtype != i32 or col.dtype != i32 or frontier.dtype != i32:
-        raise RuntimeError("rowptr, col, and frontier must be int32")
-    if x.dtype != torch.float32:
-        raise RuntimeError("x must be float32")
-    if rowptr.dim() != 1 or col.dim() != 1 or x.dim() != 2 or frontier.dim() != 1:
-        raise RuntimeError("expected rowptr[N+1], col[E], x[N,D], and frontier[B]")
-    if not (x.is_contiguous() and rowptr.is_contiguous() and col.is_contiguous()
-            and frontier.is_contiguous()):
-        raise RuntimeError("all inputs must be contiguous")
-    if rowptr.numel() != x.size(0) + 1:
-        raise RuntimeError("rowptr length must equal N+1")
 
 
 def _as_int64(value, what: str) -> int:
@@ -92,13 +80,6 @@ def _as_seed(value) -> int:
     if not 0 <= v < _U64:
         raise TypeError("replay_seed must be an integer in [0, 2**64)")
     return v
-
-
-def _check_fanout_1hop(fanout: int) -> None:
-    if fanout < 0:
-        raise RuntimeError("fanout must be non-negative")
-    if fanout > _lib.MAX_FANOUT_1HOP:
-        raise RuntimeError(f"fanout exceeds the supported maximum of {_lib.MAX_FANOUT_1HOP}")
 
 
 def _check_fanout_2hop(fanout1: int, fanout2: int) -> None:
@@ -156,98 +137,23 @@ def _ptr(t):
     return t.data_ptr() if t is not None else None
 
 
-def _zeroed(num_nodes: int, dim: int, device: torch.device, stream: int) -> torch.Tensor:
-    grad = torch.empty((num_nodes, dim), dtype=torch.float32, device=device)
-    _lib.check(_L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fsa_fill_zero_f32")
-    return grad
-
-
-def _grad_buffer(zeroed, num_nodes, dim, device, stream) -> torch.Tensor:
-    """The dense gradient: the buffer the forward already zeroed, else a new
-    zero-filled one (the reference's at::zeros, fuseop/binding.cpp:137, :220)."""
-    if zeroed is not None and tuple(zeroed.shape) == (num_nodes, dim) and zeroed.device == device:
-        return zeroed
-    return _zeroed(num_nodes, dim, device, stream)
-
-
-# ---------------------------------------------------------------------------
-# Backward launch wrappers over ctypes (fuseop/binding.cpp:119-145, :200-231):
-# the public functions' autograd runs in the C++ binding; these serve direct
-# replays of saved ids.
-# ---------------------------------------------------------------------------
-
-def _backward_1hop(samples, takes, grad_out, num_nodes):
-    if not (samples.is_cuda and takes.is_cuda and grad_out.is_cuda):
-        raise RuntimeError("backward inputs must be CUDA tensors")
-    if samples.dtype != torch.int32 or takes.dtype != torch.int32:
-        raise RuntimeError("samples and takes must be int32")
-    if not (samples.device == takes.device == grad_out.device):
-        raise RuntimeError("backward inputs must be on the same CUDA device")
-    if grad_out.dtype != torch.float32 or grad_out.dim() != 2:
-        raise RuntimeError("grad_out must be a float32 matrix")
-    if (samples.dim() != 2 or takes.dim() != 1 or samples.size(0) != grad_out.size(0)
-            or takes.size(0) != grad_out.size(0)):
-        raise RuntimeError("saved sample shapes do not match grad_out")
-    if not (samples.is_contiguous() and takes.is_contiguous() and grad_out.is_contiguous()):
-        raise RuntimeError("backward inputs must be contiguous")
-    num_nodes = _as_int64(num_nodes, "num_nodes")
-    if num_nodes < 0:
-        raise RuntimeError("num_nodes must be non-negative")
-    B, D = grad_out.shape
-    with _DeviceGuard(grad_out.device):
-        stream = _stream_handle(grad_out.device)
-        grad_x = _zeroed(num_nodes, D, grad_out.device, stream)
-        if B == 0 or samples.size(1) == 0:
-            return grad_x
-        status = _L.fsa_sample_agg_backward(
-            samples.data_ptr(), takes.data_ptr(), grad_out.data_ptr(), B, D, samples.size(1),
-            grad_x.data_ptr(), num_nodes, stream)
-        _lib.check(status, "fsa_sample_agg_backward")
-    return grad_x
-
-
-def _backward_2hop(grad_out, samples1, samples2, num_nodes, zeroed=None):
-    if not (grad_out.is_cuda and samples1.is_cuda and samples2.is_cuda):
-        raise RuntimeError("backward inputs must be CUDA tensors")
-    if (grad_out.dtype != torch.float32 or samples1.dtype != torch.int32
-            or samples2.dtype != torch.int32):
-        raise RuntimeError("invalid backward input dtypes")
-    if (grad_out.dim() != 2 or samples1.dim() != 2 or samples2.dim() != 3
-            or samples1.size(0) != grad_out.size(0) or samples2.size(0) != grad_out.size(0)
-            or samples2.size(1) != samples1.size(1)):
-        raise RuntimeError("saved sample shapes do not match grad_out")
-    if not (grad_out.device == samples1.device == samples2.device):
-        raise RuntimeError("backward inputs must be on the same CUDA device")
-    if not (grad_out.is_contiguous() and samples1.is_contiguous() and samples2.is_contiguous()):
-        raise RuntimeError("backward inputs must be contiguous")
-    num_nodes = _as_int64(num_nodes, "num_nodes")
-    if num_nodes < 0:
-        raise RuntimeError("num_nodes must be non-negative")
-    B, D = grad_out.shape
-    f1, f2 = samples1.size(1), samples2.size(2)
-    with _DeviceGuard(grad_out.device):
-        stream = _stream_handle(grad_out.device)
-        grad_x = _grad_buffer(zeroed, num_nodes, D, grad_out.device, stream)
-        if B == 0 or f1 == 0 or f2 == 0:
-            return grad_x
-        status = _L.fsa_sample_agg_2hop_backward(
-            grad_out.data_ptr(), samples1.data_ptr(), samples2.data_ptr(), B, D, f1, f2,
-            grad_x.data_ptr(), num_nodes, stream)
-        _lib.check(status, "fsa_sample_agg_2hop_backward")
-    return grad_x
-
-
 # ---------------------------------------------------------------------------
 # Public API (fuseop/__init__.py:75-206)
 # ---------------------------------------------------------------------------
 
 def fused_sample_agg(rowptr, col, x, frontier, fanout, replay_seed=1234, save_indices=False,
-                     *, batch_offset=0):
+                     *, batch_offset=0, grad_buffer=None):
     """Return the sampled 1-hop neighbor mean for each frontier node."""
     _check_python_inputs(rowptr, col, x, frontier)
-    return _C.sample_agg(rowptr, col, x, frontier, _as_int64(fanout, "fanout"),
-                         _as_seed(replay_seed), bool(save_indices),
-                         _as_int64(batch_offset, "batch_offset"))
+    fanout = _as_int64(fanout, "fanout")
+    seed = _as_seed(replay_seed)
+    offset = _as_int64(batch_offset, "batch_offset")
+    if grad_buffer is not None:
+        out, ids, flag = _C.sample_agg_into(rowptr, col, x, frontier, fanout, seed, offset,
+                                            _buffer_tensor(grad_buffer))
+        grad_buffer._record(ids, flag)
+        return out
+    return _C.sample_agg(rowptr, col, x, frontier, fanout, seed, bool(save_indices), offset)
 
 
 def fused_sample_agg_with_samples(rowptr, col, x, frontier, fanout, replay_seed=1234,
@@ -264,12 +170,20 @@ def fused_sample_agg_with_samples(rowptr, col, x, frontier, fanout, replay_seed=
 
 
 def fused_sample_agg_2hop(rowptr, col, x, frontier, fanout1, fanout2, replay_seed=1234,
-                          save_indices=False, *, batch_offset=0):
+                          save_indices=False, *, batch_offset=0, grad_buffer=None):
     """Return the nested sampled 2-hop neighbor mean for each frontier node."""
     _check_python_inputs(rowptr, col, x, frontier)
-    return _C.sample_agg_2hop(rowptr, col, x, frontier, _as_int64(fanout1, "fanout1"),
-                              _as_int64(fanout2, "fanout2"), _as_seed(replay_seed),
-                              bool(save_indices), _as_int64(batch_offset, "batch_offset"))
+    f1 = _as_int64(fanout1, "fanout1")
+    f2 = _as_int64(fanout2, "fanout2")
+    seed = _as_seed(replay_seed)
+    offset = _as_int64(batch_offset, "batch_offset")
+    if grad_buffer is not None:
+        out, ids, flag = _C.sample_agg_2hop_into(rowptr, col, x, frontier, f1, f2, seed, offset,
+                                                 _buffer_tensor(grad_buffer))
+        grad_buffer._record(ids, flag)
+        return out
+    return _C.sample_agg_2hop(rowptr, col, x, frontier, f1, f2, seed, bool(save_indices),
+                              offset)
 
 
 def fused_sample_agg_2hop_with_samples(rowptr, col, x, frontier, fanout1, fanout2,
@@ -284,6 +198,72 @@ def fused_sample_agg_2hop_with_samples(rowptr, col, x, frontier, fanout1, fanout
                                            _as_int64(fanout1, "fanout1"),
                                            _as_int64(fanout2, "fanout2"), _as_seed(replay_seed),
                                            _as_int64(batch_offset, "batch_offset"))
+
+
+# ---------------------------------------------------------------------------
+# Persistent gradient buffer (opt-in; no counterpart in the reference)
+# ---------------------------------------------------------------------------
+
+class PersistentGradient:
+    """A feature-table gradient kept across steps and cleared row by row.
+
+    The reference's backward hands autograd a fresh dense N x D gradient on
+    every call (at::zeros, fuseop/binding.cpp:137, :220): 4 N D bytes of
+    zero fill per step although a step touches only the sampled rows.
+    Passing ``grad_buffer=buf`` to ``fused_sample_agg`` or
+    ``fused_sample_agg_2hop`` makes the backward add into ``buf.grad``
+    instead, and autograd then produces no gradient for ``x`` from that call.
+    ``buf.zero_()`` clears the rows that the calls since the previous
+    ``zero_()`` sample -- their saved ids -- rather than the whole table.
+
+    ``buf.grad`` is one tensor for the buffer's lifetime.  To train through
+    an optimizer, alias it once (``x.grad = buf.grad``) and call
+    ``buf.zero_()`` where ``optimizer.zero_grad()`` would go (never
+    ``zero_grad(set_to_none=True)``, which drops the alias).  Calls are
+    stream-ordered on the current stream like the rest of the API.
+
+    Rows of a forward whose backward has not run yet are cleared again by
+    every later ``zero_()`` until that backward has run (or its graph has
+    been freed), so ``zero_()`` may sit anywhere between steps.
+    """
+
+    def __init__(self, x: torch.Tensor):
+        if not (x.is_cuda and x.dim() == 2):
+            raise ValueError("PersistentGradient needs the 2-D CUDA feature tensor")
+        with _DeviceGuard(x.device):
+            self.grad = torch.empty(tuple(x.shape), dtype=torch.float32, device=x.device)
+            _lib.check(_L.fsa_fill_zero_f32(self.grad.data_ptr(), self.grad.numel(),
+                                            _stream_handle(x.device)), "fsa_fill_zero_f32")
+        self._touched: list[tuple[torch.Tensor, torch.Tensor]] = []
+
+    def _record(self, ids, flag) -> None:
+        if ids is not None:
+            self._touched.append((ids, flag))
+
+    @property
+    def pending_rows(self) -> int:
+        """Saved-id entries (rows, with repeats and -1 padding) that the next
+        ``zero_()`` will clear."""
+        return sum(int(ids.numel()) for ids, _ in self._touched)
+
+    def zero_(self) -> "PersistentGradient":
+        """Zeroes the rows touched since the last call (one fsa_zero_rows_f32
+        launch per recorded call)."""
+        keep = []
+        for ids, flag in self._touched:
+            _C.zero_rows(self.grad, ids)
+            # still awaiting its backward, and its graph (which holds the
+            # other reference to the flag) is alive
+            if int(flag[0]) != 0 and flag._use_count() > 1:
+                keep.append((ids, flag))
+        self._touched = keep
+        return self
+
+
+def _buffer_tensor(buf) -> torch.Tensor:
+    if not isinstance(buf, PersistentGradient):
+        raise TypeError("grad_buffer must be a fusesampleagg_b200.PersistentGradient")
+    return buf.grad
 
 
 def launch_count() -> int:

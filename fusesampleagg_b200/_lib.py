@@ -57,6 +57,7 @@ SIGNATURES = {
     "fsa_sample_agg_2hop_backward_sorted": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p, ctypes.c_size_t, _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),
+    "fsa_zero_rows_f32": (_int, [_p, _i64, _i64, _p, _i64, _p]),
     "fsa_phase_timing": (_int, [_int]),
     "fsa_phase_times": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
     "fsa_ipc_export": (_int, [_p, _p, ctypes.POINTER(_u64)]),

@@ -76,6 +76,22 @@ def nvcc_command(output: Path, verbose_ptxas: bool = False) -> list[str]:
     return cmd
 
 
+def cxx_path() -> str:
+    """The binding's C++ compiler: FSA_CXX, else the g++ on PATH.
+
+    Not $CXX: the binding throws C++ exceptions (TORCH_CHECK) that unwind
+    through libc10 / libtorch, so it must be built by the plain system
+    toolchain those libraries were linked against.  A CXX wrapper that adds
+    its own -B support-library directories produced a binding whose
+    TORCH_CHECK failures with formatted messages crashed the process
+    (SIGSEGV) instead of raising RuntimeError.
+    """
+    cxx = os.environ.get("FSA_CXX") or shutil.which("g++")
+    if cxx is None:
+        raise RuntimeError("g++ not found; set FSA_CXX")
+    return cxx
+
+
 def ext_command(output: Path) -> list[str]:
     """g++ line of the torch binding: torch's include and library paths and
     C++ ABI setting, linked to libfsa_sm100.so found beside it at run time."""
@@ -84,7 +100,7 @@ def ext_command(output: Path) -> list[str]:
 
     abi = int(bool(torch._C._GLIBCXX_USE_CXX11_ABI))
     cmd = [
-        os.environ.get("CXX", "g++"),
+        cxx_path(),
         "-std=c++17",
         "-O2",
         "-shared",

@@ -848,6 +848,7 @@ struct Gather2Args {
   int32_t* samples2;     // optional id output; may alias win2
   float* out;
   int dchunk;            // feature tile width (multiple of the vector width)
+  int ids_ready;         // win2 already holds the ids (fsa_2hop_resolve_kernel ran)
   RowShards xs;          // sharded feature rows (kSharded kernels only)
 };
 
@@ -906,7 +907,9 @@ __global__ void __launch_bounds__(kThreadsGather, 4)
       const int j = e - i * k2;
       const int64_t r = b * k1 + i;
       int32_t id = -1;
-      if (j < __ldg(a.mtake + r)) {
+      if (a.ids_ready) {
+        id = a.win2[b * k12 + e];
+      } else if (j < __ldg(a.mtake + r)) {
         const int w = a.win2[b * k12 + e];
         id = __ldg(a.col + static_cast<int64_t>(__ldg(a.mbeg + r)) + (w >= 0 ? w : j));
       }
@@ -981,6 +984,49 @@ __global__ void __launch_bounds__(kThreadsGather, 4)
       __syncthreads();
     }
     __syncthreads();
+  }
+}
+
+// Winners -> second-hop ids for every (root, slot, j) of the batch, one
+// thread per entry, written over the winner (win2 is samples2 when the
+// caller asked for ids, else workspace).  Slot j of a row holds col[winner],
+// or col[j] if no draw replaced it -- the serial loop's final reservoir
+// (fused_sample_agg.cu:40-56); -1 past the row's take.  Used for large
+// batches (kResolveMinRows second-hop rows and up): resolving all ids in one
+// flat pass takes the dependent col lookups out of every root's chain in the
+// gather kernel that follows (measured, 65,536 roots at 15 x 10 with
+// D = 128: gather 994 -> 942 us including this kernel).  For small batches
+// the extra launch costs more than it saves (1024 roots: 24.7 -> 25.7 us),
+// and the gather resolves the ids itself.
+struct Resolve2Args {
+  const int32_t* col;
+  int64_t num_nodes;
+  int64_t entries;  // batch_size * fanout1 * fanout2
+  int fanout2;
+  const int32_t* mbeg;   // [B*k1]
+  const int32_t* mtake;  // [B*k1]
+  int32_t* win2;         // [B][k1][k2] winners in, ids out
+};
+
+constexpr int kThreadsResolve = 256;
+constexpr int64_t kResolveMinRows = 32768;
+
+__global__ void __launch_bounds__(kThreadsResolve) fsa_2hop_resolve_kernel(const Resolve2Args a) {
+  // A programmatic dependent of the draw kernel: the winners are its results.
+  wait_prerequisites();
+  launch_dependents();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < a.entries;
+       e += stride) {
+    const int64_t r = e / a.fanout2;
+    const int j = static_cast<int>(e - r * a.fanout2);
+    int32_t id = -1;
+    if (j < __ldg(a.mtake + r)) {
+      const int w = a.win2[e];
+      id = __ldg(a.col + static_cast<int64_t>(__ldg(a.mbeg + r)) + (w >= 0 ? w : j));
+      if (id >= a.num_nodes) flag_status(FSA_STATUS_BAD_NEIGHBOR);
+    }
+    a.win2[e] = id;
   }
 }
 
@@ -1280,6 +1326,29 @@ __global__ void __launch_bounds__(kThreadsFill)
   }
 }
 
+// Zeroes table rows rows[k] (0 <= rows[k] < num_rows; others, such as the -1
+// padding of saved ids, are skipped): one warp per listed row, V-float
+// stores.  Plain (L2-allocating) stores: the rows are about to receive the
+// backward's red.add, which then hits L2.  A row listed twice is written
+// twice with the same zeros.
+template <int V>
+__global__ void __launch_bounds__(kThreadsFill)
+    fsa_zero_rows_kernel(float* __restrict__ table, int64_t num_rows, int64_t dim,
+                         const int32_t* __restrict__ rows, int64_t count) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t dvec = dim / V;
+  VecF<V> z;
+  vzero(z);
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       e < count; e += warps) {
+    const int32_t r = __ldg(rows + e);
+    if (r < 0 || r >= num_rows) continue;
+    float* p = table + static_cast<int64_t>(r) * dim;
+    for (int64_t v = lane; v < dvec; v += 32) store_vec(p + v * V, z);
+  }
+}
+
 __global__ void __launch_bounds__(kThreadsFill)
     fsa_fill_zero_scalar_kernel(float* __restrict__ dst, int64_t count) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -1541,15 +1610,14 @@ size_t fsa_sample_agg_2hop_workspace_size(int64_t batch_size, int32_t fanout1,
   return ws2_layout(batch_size, fanout1, fanout2, has_samples1 == 0, has_samples2 == 0).total;
 }
 
-// The 2-hop forward; `xs` (optional) reads the feature rows from a shard
-// table instead of x.
-static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_nodes,
-                        int64_t num_edges, const float* x, int64_t feature_dim,
-                        const int32_t* frontier, int64_t batch_size, int64_t batch_offset,
-                        int32_t fanout1, int32_t fanout2, uint64_t seed, float* out,
-                        int32_t* samples1, int32_t* samples2, void* workspace,
-                        size_t workspace_bytes, float* zero_fill, int64_t zero_count,
-                        void* stream, const RowShards* xs) {
+// Argument checks of the 2-hop forward that need no CUDA call (everything
+// but the workspace).
+static int check_forward_2hop_args(const int32_t* rowptr, const int32_t* col, int64_t num_nodes,
+                                   int64_t num_edges, const float* x, int64_t feature_dim,
+                                   const int32_t* frontier, int64_t batch_size,
+                                   int64_t batch_offset, int32_t fanout1, int32_t fanout2,
+                                   const float* out, const float* zero_fill,
+                                   int64_t zero_count) {
   if (fanout1 < 0 || fanout2 < 0 || batch_size < 0 || feature_dim < 0 ||
       num_nodes < 0 || num_edges < 0 || batch_offset < 0 || zero_count < 0 ||
       (zero_count > 0 && zero_fill == nullptr)) {
@@ -1560,11 +1628,31 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
     return FSA_ERR_INVALID_ARGUMENT;
   }
   const bool work = batch_size > 0 && fanout1 > 0 && fanout2 > 0;
+  if (work && (rowptr == nullptr || frontier == nullptr || (num_edges > 0 && col == nullptr) ||
+               (feature_dim > 0 && (out == nullptr || (num_nodes > 0 && x == nullptr))))) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  return FSA_OK;
+}
+
+// The 2-hop forward; `xs` (optional) reads the feature rows from a shard
+// table instead of x.
+static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_nodes,
+                        int64_t num_edges, const float* x, int64_t feature_dim,
+                        const int32_t* frontier, int64_t batch_size, int64_t batch_offset,
+                        int32_t fanout1, int32_t fanout2, uint64_t seed, float* out,
+                        int32_t* samples1, int32_t* samples2, void* workspace,
+                        size_t workspace_bytes, float* zero_fill, int64_t zero_count,
+                        void* stream, const RowShards* xs) {
+  const int arg_status =
+      check_forward_2hop_args(rowptr, col, num_nodes, num_edges, x, feature_dim, frontier,
+                              batch_size, batch_offset, fanout1, fanout2, out, zero_fill,
+                              zero_count);
+  if (arg_status != FSA_OK) return arg_status;
+  const bool work = batch_size > 0 && fanout1 > 0 && fanout2 > 0;
   const Ws2 wl = ws2_layout(batch_size, fanout1, fanout2, samples1 == nullptr,
                             samples2 == nullptr);
-  if (work && (rowptr == nullptr || frontier == nullptr || (num_edges > 0 && col == nullptr) ||
-               (feature_dim > 0 && (out == nullptr || (num_nodes > 0 && x == nullptr))) ||
-               workspace == nullptr || workspace_bytes < wl.total || !aligned(workspace, 256))) {
+  if (work && (workspace == nullptr || workspace_bytes < wl.total || !aligned(workspace, 256))) {
     return FSA_ERR_INVALID_ARGUMENT;
   }
   // The zero fill rides along in the draw kernel (float4 stores); a buffer
@@ -1629,10 +1717,21 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
   if (st == FSA_OK) st = pe.mark(3, s);
   if (st != FSA_OK) return st;
   Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
-                 mtake, win2, samples2, out, dchunk, RowShards{}};
+                 mtake, win2, samples2, out, dchunk, 0, RowShards{}};
+  if (xs != nullptr) ga.xs = *xs;
+  if (batch_size * fanout1 >= kResolveMinRows) {
+    // winners -> ids in place (win2 is samples2 when ids were requested)
+    const int64_t entries = batch_size * fanout1 * fanout2;
+    const Resolve2Args ra{col, num_nodes, entries, fanout2, mbeg, mtake, win2};
+    st = launch_dependent(fsa_2hop_resolve_kernel,
+                          grid_for((entries + kThreadsResolve - 1) / kThreadsResolve),
+                          kThreadsResolve, 0, s, ra);
+    if (st != FSA_OK) return st;
+    ga.samples2 = nullptr;  // the ids are already in place
+    ga.ids_ready = 1;
+  }
   const int ggrid = grid_for(batch_size);
   if (xs != nullptr) {
-    ga.xs = *xs;
     switch (vec) {
       case 4: st = launch(fsa_2hop_gather_kernel<4, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
       case 2: st = launch(fsa_2hop_gather_kernel<2, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
@@ -1872,6 +1971,25 @@ int fsa_fill_zero_f32(float* dst, int64_t count, void* stream) {
   return check_launch();
 }
 
+int fsa_zero_rows_f32(float* table, int64_t num_rows, int64_t dim, const int32_t* rows,
+                      int64_t count, void* stream) {
+  if (num_rows < 0 || dim < 0 || count < 0 || (count > 0 && rows == nullptr) ||
+      (num_rows > 0 && dim > 0 && count > 0 && table == nullptr)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  if (count == 0 || num_rows == 0 || dim == 0) return FSA_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int vec = pick_vec(dim, table, table);
+  const int64_t per_cta = kThreadsFill / 32;
+  const int grid = grid_for((count + per_cta - 1) / per_cta);
+  switch (vec) {
+    case 4: fsa_zero_rows_kernel<4><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+    case 2: fsa_zero_rows_kernel<2><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+    default: fsa_zero_rows_kernel<1><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+  }
+  return check_launch();
+}
+
 int fsa_phase_timing(int enable) {
   std::lock_guard<std::mutex> lock(g_timing_mu);
   if (enable) {
@@ -2040,7 +2158,10 @@ std::atomic<void*> g_scratch_addr[kScratchDevices];
 
 // Device address of g_ws2_scratch on the current device.  The first call
 // per device runs cudaGetSymbolAddress (which also loads the module there);
-// later calls read the cached pointer.
+// later calls read the cached pointer.  The cache is per device ordinal and
+// is never refreshed: a device reset (cudaDeviceReset, or anything else that
+// destroys the primary context) may reload the module at another address,
+// so the entry point is not for use across such a reset.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -2075,18 +2196,22 @@ int fsa_sample_agg_2hop_forward_noalloc(const int32_t* rowptr, const int32_t* co
                                         int32_t* samples1, int32_t* samples2,
                                         float* zero_fill, int64_t zero_count,
                                         void* stream) {
-  const bool work = batch_size > 0 && fanout1 > 0 && fanout2 > 0 &&
-                    static_cast<int64_t>(fanout1) + static_cast<int64_t>(fanout1) * fanout2 <=
-                        FSA_MAX_2HOP_ENTRIES;
+  // The workspace entry point's argument checks first (host only), so that
+  // a call with bad arguments is told so whatever its size.
+  const int arg_status =
+      check_forward_2hop_args(rowptr, col, num_nodes, num_edges, x, feature_dim, frontier,
+                              batch_size, batch_offset, fanout1, fanout2, out, zero_fill,
+                              zero_count);
+  if (arg_status != FSA_OK) return arg_status;
+  const bool work = batch_size > 0 && fanout1 > 0 && fanout2 > 0;
   if (!work) {
-    // Nothing to sample (or arguments the workspace entry point rejects):
-    // no scratch is used.
+    // Nothing to sample: no scratch is used.
     return fsa_sample_agg_2hop_forward(rowptr, col, num_nodes, num_edges, x, feature_dim,
                                        frontier, batch_size, batch_offset, fanout1, fanout2,
                                        seed, out, samples1, samples2, nullptr, 0, zero_fill,
                                        zero_count, stream);
   }
-  // Size limit first, before any CUDA call.  A batch with more roots than
+  // Then the size limit, before any CUDA call.  A batch with more roots than
   // scratch bytes cannot fit (8 bytes per root alone); checking that first
   // keeps the layout arithmetic far from overflow.
   if (batch_size > static_cast<int64_t>(FSA_NOALLOC_SCRATCH_BYTES) ||

@@ -20,8 +20,10 @@
 #include <torch/python.h>
 
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <tuple>
+#include <unordered_map>
 #include <vector>
 
 #include "fsa_sm100.h"
@@ -299,10 +301,59 @@ Tensor backward_2hop(const Tensor& grad_out, const Tensor& s1, const Tensor& s2,
   return grad_x;
 }
 
+// Dense gradient buffers that 2-hop forwards allocated (and zeroed) ahead of
+// their backward, one per feature table at most.  A forward allocates one
+// only when no other forward over the same table holds one that its
+// backward has not taken yet; later forwards leave the fill to their own
+// backward, as the reference does for every call (fuseop/binding.cpp:220).
+// So k forwards before their backwards (gradient accumulation, several
+// encoder calls per step) hold at most one extra N x D buffer, not k.  The
+// table is keyed by the feature tensor's TensorImpl and holds weak
+// references: a buffer whose graph was dropped without a backward is freed
+// with it and no longer counts.
+class ForwardBuffers {
+ public:
+  using Weak = c10::weak_intrusive_ptr<c10::TensorImpl, c10::UndefinedTensorImpl>;
+
+  // A new zeroing target for a forward over `x`, or an undefined tensor when
+  // another forward over x still holds one.
+  Tensor claim(const Tensor& x) {
+    const std::lock_guard<std::mutex> lock(mu_);
+    for (auto it = held_.begin(); it != held_.end();) {
+      it = it->second.expired() ? held_.erase(it) : std::next(it);
+    }
+    const auto* key = x.unsafeGetTensorImpl();
+    if (held_.count(key) != 0) return Tensor();
+    Tensor buf = at::empty({x.size(0), x.size(1)}, x.options().dtype(at::kFloat));
+    held_.emplace(key, Weak(buf.getIntrusivePtr()));
+    return buf;
+  }
+
+  // The backward of the forward over the table `key` took `buf`.
+  void release(int64_t key, const Tensor& buf) {
+    const std::lock_guard<std::mutex> lock(mu_);
+    auto it = held_.find(reinterpret_cast<const c10::TensorImpl*>(key));
+    if (it != held_.end() && it->second.lock().get() == buf.unsafeGetTensorImpl()) {
+      held_.erase(it);
+    }
+  }
+
+ private:
+  std::mutex mu_;
+  std::unordered_map<const c10::TensorImpl*, Weak> held_;
+};
+
+ForwardBuffers& forward_buffers() {
+  static ForwardBuffers* b = new ForwardBuffers();  // never destroyed: used at exit
+  return *b;
+}
+
 // fuseop/__init__.py:108-161.  When the backward will need the dense feature
-// gradient, the forward allocates it and the library's draw kernel zeroes it
-// (bound by integer issue, it leaves HBM bandwidth idle that the fill uses);
-// the reference zero-fills inside the backward (fuseop/binding.cpp:220).
+// gradient, the forward allocates it (at most one pending per table, see
+// ForwardBuffers) and the library's draw kernel zeroes it (bound by integer
+// issue, it leaves HBM bandwidth idle that the fill uses); the reference
+// zero-fills inside the backward (fuseop/binding.cpp:220), as this backward
+// does when the forward held no buffer.
 struct SampleAgg2Hop : public torch::autograd::Function<SampleAgg2Hop> {
   static Tensor forward(AutogradContext* ctx, const Tensor& rowptr, const Tensor& col,
                         const Tensor& x, const Tensor& frontier, int64_t f1, int64_t f2,
@@ -310,7 +361,7 @@ struct SampleAgg2Hop : public torch::autograd::Function<SampleAgg2Hop> {
     Tensor grad_buffer;
     if (capture && grad_needed) {
       TORCH_CHECK(x.is_cuda() && x.dim() == 2, "expected x[N,D] on a CUDA device");
-      grad_buffer = at::empty({x.size(0), x.size(1)}, x.options().dtype(at::kFloat));
+      grad_buffer = forward_buffers().claim(x);
     }
     auto [out, s1, s2] =
         forward_2hop(rowptr, col, x, frontier, f1, f2, seed, capture, batch_offset, grad_buffer);
@@ -318,7 +369,10 @@ struct SampleAgg2Hop : public torch::autograd::Function<SampleAgg2Hop> {
     ctx->saved_data["capture"] = capture;
     ctx->saved_data["grad_needed"] = grad_needed;
     ctx->saved_data["num_nodes"] = x.size(0);
-    if (grad_buffer.defined()) ctx->saved_data["grad_buffer"] = grad_buffer;
+    if (grad_buffer.defined()) {
+      ctx->saved_data["grad_buffer"] = grad_buffer;
+      ctx->saved_data["table"] = reinterpret_cast<int64_t>(x.unsafeGetTensorImpl());
+    }
     return out;
   }
 
@@ -331,6 +385,7 @@ struct SampleAgg2Hop : public torch::autograd::Function<SampleAgg2Hop> {
       if (it != ctx->saved_data.end()) {
         buf = it->second.toTensor();
         ctx->saved_data.erase(it);
+        forward_buffers().release(ctx->saved_data["table"].toInt(), buf);
       }
       grad_x = backward_2hop(grads[0].contiguous(), saved[0], saved[1],
                              ctx->saved_data["num_nodes"].toInt(), buf);
@@ -339,6 +394,143 @@ struct SampleAgg2Hop : public torch::autograd::Function<SampleAgg2Hop> {
             Tensor(), Tensor()};
   }
 };
+
+// ---------------------------------------------------------------------------
+// Persistent gradient buffer (opt-in; no counterpart in the reference)
+//
+// The reference's backward returns a fresh dense N x D gradient every call
+// (at::zeros, fuseop/binding.cpp:137, :220) -- 4 N D bytes of fill per step
+// for a sparse update.  With a caller-held buffer the backward instead adds
+// into that buffer and returns no gradient for x; the forward returns its
+// saved ids and a host flag as well, so that the caller can clear exactly
+// the rows the backward will touch (fsa_zero_rows_f32) instead of all N.
+// The flag is 1 until the backward has added into the buffer.
+// ---------------------------------------------------------------------------
+
+void check_grad_into(const Tensor& into, const Tensor& x) {
+  TORCH_CHECK(into.sizes() == x.sizes(), "grad_buffer shape must equal the features' shape (",
+              into.sizes(), " vs ", x.sizes(), ")");
+  TORCH_CHECK(into.is_cuda() && into.device() == x.device(),
+              "grad_buffer must be on the features' CUDA device");
+  TORCH_CHECK(into.scalar_type() == at::kFloat && into.dim() == 2 && into.is_contiguous(),
+              "grad_buffer must be a contiguous float32 matrix");
+}
+
+Tensor pending_flag() { return at::ones({1}, at::TensorOptions().dtype(at::kInt)); }
+
+struct SampleAgg2HopInto : public torch::autograd::Function<SampleAgg2HopInto> {
+  static variable_list forward(AutogradContext* ctx, const Tensor& rowptr, const Tensor& col,
+                               const Tensor& x, const Tensor& frontier, int64_t f1, int64_t f2,
+                               uint64_t seed, int64_t batch_offset, const Tensor& into) {
+    auto [out, s1, s2] =
+        forward_2hop(rowptr, col, x, frontier, f1, f2, seed, true, batch_offset, Tensor());
+    Tensor flag = pending_flag();
+    ctx->save_for_backward({s1, s2});
+    ctx->saved_data["into"] = into;
+    ctx->saved_data["flag"] = flag;
+    ctx->mark_non_differentiable({s2, flag});
+    return {out, s2, flag};
+  }
+
+  static variable_list backward(AutogradContext* ctx, variable_list grads) {
+    auto saved = ctx->get_saved_variables();
+    Tensor into = ctx->saved_data["into"].toTensor();
+    if (grads[0].defined()) {
+      const Tensor g = grads[0].contiguous();
+      const c10::cuda::CUDAGuard guard(g.device());
+      check_status(fsa_sample_agg_2hop_backward(
+                       g.data_ptr<float>(), saved[0].data_ptr<int32_t>(),
+                       saved[1].data_ptr<int32_t>(), g.size(0), g.size(1),
+                       static_cast<int32_t>(saved[0].size(1)),
+                       static_cast<int32_t>(saved[1].size(2)), into.data_ptr<float>(),
+                       into.size(0), stream_of(g)),
+                   "fsa_sample_agg_2hop_backward");
+    }
+    ctx->saved_data["flag"].toTensor().data_ptr<int32_t>()[0] = 0;
+    return variable_list(9);
+  }
+};
+
+std::vector<Tensor> sample_agg_2hop_into(const Tensor& rowptr, const Tensor& col,
+                                         const Tensor& x, const Tensor& frontier, int64_t f1,
+                                         int64_t f2, uint64_t seed, int64_t batch_offset,
+                                         const Tensor& into) {
+  check_grad_into(into, x);
+  if (!(at::GradMode::is_enabled() && x.requires_grad())) {
+    auto r = forward_2hop(rowptr, col, x, frontier, f1, f2, seed, false, batch_offset, Tensor());
+    return {std::get<0>(r), Tensor(), Tensor()};
+  }
+  return SampleAgg2HopInto::apply(rowptr, col, x, frontier, f1, f2, seed, batch_offset, into);
+}
+
+struct SampleAgg1HopInto : public torch::autograd::Function<SampleAgg1HopInto> {
+  static variable_list forward(AutogradContext* ctx, const Tensor& rowptr, const Tensor& col,
+                               const Tensor& x, const Tensor& frontier, int64_t fanout,
+                               uint64_t seed, int64_t batch_offset, const Tensor& into) {
+    auto r = forward_1hop(rowptr, col, x, frontier, fanout, seed, true, batch_offset);
+    Tensor flag = pending_flag();
+    ctx->save_for_backward({r[1], r[2]});
+    ctx->saved_data["into"] = into;
+    ctx->saved_data["flag"] = flag;
+    ctx->mark_non_differentiable({r[1], flag});
+    return {r[0], r[1], flag};
+  }
+
+  static variable_list backward(AutogradContext* ctx, variable_list grads) {
+    auto saved = ctx->get_saved_variables();
+    Tensor into = ctx->saved_data["into"].toTensor();
+    if (grads[0].defined() && saved[0].numel() > 0) {
+      const Tensor g = grads[0].contiguous();
+      const c10::cuda::CUDAGuard guard(g.device());
+      check_status(fsa_sample_agg_backward(saved[0].data_ptr<int32_t>(),
+                                           saved[1].data_ptr<int32_t>(), g.data_ptr<float>(),
+                                           g.size(0), g.size(1),
+                                           static_cast<int32_t>(saved[0].size(1)),
+                                           into.data_ptr<float>(), into.size(0), stream_of(g)),
+                   "fsa_sample_agg_backward");
+    }
+    ctx->saved_data["flag"].toTensor().data_ptr<int32_t>()[0] = 0;
+    return variable_list(8);
+  }
+};
+
+std::vector<Tensor> sample_agg_into(const Tensor& rowptr, const Tensor& col, const Tensor& x,
+                                    const Tensor& frontier, int64_t fanout, uint64_t seed,
+                                    int64_t batch_offset, const Tensor& into) {
+  check_grad_into(into, x);
+  if (!(at::GradMode::is_enabled() && x.requires_grad())) {
+    auto r = forward_1hop(rowptr, col, x, frontier, fanout, seed, false, batch_offset);
+    return {r[0], Tensor(), Tensor()};
+  }
+  return SampleAgg1HopInto::apply(rowptr, col, x, frontier, fanout, seed, batch_offset, into);
+}
+
+// Clears rows `rows` (saved ids; -1 entries skipped) of a persistent buffer.
+void zero_rows(const Tensor& table, const Tensor& rows) {
+  TORCH_CHECK(table.is_cuda() && rows.is_cuda() && table.device() == rows.device(),
+              "zero_rows: tensors must be on one CUDA device");
+  TORCH_CHECK(table.scalar_type() == at::kFloat && table.dim() == 2 && table.is_contiguous(),
+              "zero_rows: table must be a contiguous float32 matrix");
+  TORCH_CHECK(rows.scalar_type() == at::kInt && rows.is_contiguous(),
+              "zero_rows: rows must be contiguous int32");
+  const c10::cuda::CUDAGuard guard(table.device());
+  check_status(fsa_zero_rows_f32(table.data_ptr<float>(), table.size(0), table.size(1),
+                                 rows.data_ptr<int32_t>(), rows.numel(), stream_of(table)),
+               "fsa_zero_rows_f32");
+}
+
+// The reference binding's backward entry points (fuseop/binding.cpp:119-145,
+// :200-231, exported at :236-242): a saved-index replay into a fresh
+// zero-filled gradient.
+Tensor replay_backward_1hop(const Tensor& samples, const Tensor& takes, const Tensor& grad_out,
+                            int64_t num_nodes) {
+  return backward_1hop(samples, takes, grad_out, num_nodes);
+}
+
+Tensor replay_backward_2hop(const Tensor& grad_out, const Tensor& s1, const Tensor& s2,
+                            int64_t num_nodes) {
+  return backward_2hop(grad_out, s1, s2, num_nodes, Tensor());
+}
 
 Tensor sample_agg_2hop(const Tensor& rowptr, const Tensor& col, const Tensor& x,
                        const Tensor& frontier, int64_t f1, int64_t f2, uint64_t seed,
@@ -364,4 +556,9 @@ PYBIND11_MODULE(_fsa_torch, m) {
   m.def("sample_agg_with_samples", &sample_agg_with_samples);
   m.def("sample_agg_2hop", &sample_agg_2hop);
   m.def("sample_agg_2hop_with_samples", &sample_agg_2hop_with_samples);
+  m.def("sample_agg_backward", &replay_backward_1hop);
+  m.def("sample_agg_2hop_backward", &replay_backward_2hop);
+  m.def("sample_agg_into", &sample_agg_into);
+  m.def("sample_agg_2hop_into", &sample_agg_2hop_into);
+  m.def("zero_rows", &zero_rows);
 }

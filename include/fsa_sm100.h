@@ -152,6 +152,11 @@ FSA_API int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* co
  * The first call on a device does set-up: cudaGetSymbolAddress of the
  * scratch (which loads the module on that device if needed), checked and
  * then cached per device.  Make that first call before any stream capture.
+ * The cached address is not refreshed after a device reset (cudaDeviceReset
+ * or another end of the primary context), which is unsupported here.
+ *
+ * Arguments are checked as by the workspace entry point first
+ * (FSA_ERR_INVALID_ARGUMENT), then the size limit.
  * Nothing in the scratch needs to start at zero: the call's first kernel
  * writes every word the later kernels read.
  *
@@ -281,6 +286,19 @@ FSA_API int fsa_sample_agg_2hop_backward_sorted(const float* grad_out, const int
  * at::zeros({N, D}) of the reference backward (fuseop/binding.cpp:137, :220).
  */
 FSA_API int fsa_fill_zero_f32(float* dst, int64_t count, void* stream);
+
+/*
+ * Zero the rows rows[0..count) of table float32[num_rows][dim]; entries
+ * outside [0, num_rows) -- the -1 padding of saved ids -- are skipped.  The
+ * row-sparse counterpart of the fill above: a gradient buffer kept across
+ * steps is cleared by zeroing the rows the previous steps' saved ids touched
+ * (pass samples2 or samples as the row list), 4 * dim bytes per listed row
+ * instead of 4 * num_rows * dim.  No counterpart in the reference, whose
+ * backward zero-fills a fresh N x D gradient every call
+ * (fuseop/binding.cpp:137, :220).
+ */
+FSA_API int fsa_zero_rows_f32(float* table, int64_t num_rows, int64_t dim, const int32_t* rows,
+                              int64_t count, void* stream);
 
 /*
  * Per-kernel timing of fsa_sample_agg_2hop_forward, for benchmarks (no

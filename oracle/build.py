@@ -15,7 +15,9 @@ Builds two checkers:
   where the bit-exact golden vectors (tests/golden/) come from and what
   ``bench.py --impl reference`` times.
 
-Usage: ``python -m oracle.build [--ref] [--reference-root PATH]``.
+Usage: ``python -m oracle.build [--ref --reference-root PATH]``; the
+reference checkout may also be named by the FSA_REFERENCE_ROOT environment
+variable.  There is no default location.
 """
 
 from __future__ import annotations
@@ -29,7 +31,13 @@ from pathlib import Path
 ORACLE_DIR = Path(__file__).resolve().parent
 REF_OUT = ORACLE_DIR / "_ref"
 REF_PKG = REF_OUT / "fuseop"
-DEFAULT_REFERENCE_ROOT = Path("/root/reference")
+REFERENCE_ROOT_ENV = "FSA_REFERENCE_ROOT"
+
+
+def reference_root_from_env() -> Path | None:
+    """The reference checkout named by FSA_REFERENCE_ROOT, if any."""
+    v = os.environ.get(REFERENCE_ROOT_ENV)
+    return Path(v) if v else None
 
 
 def build_oracle(force: bool = False) -> Path:
@@ -45,21 +53,27 @@ def build_oracle(force: bool = False) -> Path:
     return out
 
 
-def reference_available(reference_root: Path = DEFAULT_REFERENCE_ROOT) -> bool:
-    return (reference_root / "fuseop" / "fused_sample_agg.cu").exists()
+def reference_available(reference_root: Path | None) -> bool:
+    return reference_root is not None and (reference_root / "fuseop" / "fused_sample_agg.cu").exists()
 
 
 def ref_built() -> bool:
     return any(REF_PKG.glob("_C*.so")) and (REF_PKG / "__init__.py").exists()
 
 
-def build_ref(reference_root: Path = DEFAULT_REFERENCE_ROOT, force: bool = False) -> Path | None:
+def build_ref(reference_root: Path | None, force: bool = False) -> Path | None:
     """Compiles the reference op into oracle/_ref/fuseop (None if absent)."""
     if not reference_available(reference_root):
         return None
     if ref_built() and not force:
         return REF_PKG
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0"
+    # torch's extension builder takes the host compiler from CXX; use the
+    # system g++ (a CXX wrapper with its own support-library paths built
+    # extensions whose formatted TORCH_CHECK failures crashed).
+    gxx = shutil.which("g++")
+    if gxx:
+        os.environ["CXX"] = gxx
     from torch.utils.cpp_extension import load
 
     build_dir = REF_OUT / "build"
@@ -91,10 +105,13 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--ref", action="store_true", help="also build the reference op")
     parser.add_argument("--force", action="store_true")
-    parser.add_argument("--reference-root", type=Path, default=DEFAULT_REFERENCE_ROOT)
+    parser.add_argument("--reference-root", type=Path, default=reference_root_from_env(),
+                        help=f"reference checkout (default: ${REFERENCE_ROOT_ENV})")
     args = parser.parse_args()
     print(build_oracle(force=args.force))
     if args.ref:
+        if args.reference_root is None:
+            parser.error(f"--ref needs --reference-root or ${REFERENCE_ROOT_ENV}")
         print(build_ref(args.reference_root, force=args.force))
 
 

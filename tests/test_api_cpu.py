@@ -1,6 +1,9 @@
-"""Host-side behaviour of the public API without a GPU: the reference's error
-types and messages (fuseop/__init__.py:15-29, fuseop/binding.cpp:16-53 and
-:119-135, :200-218), argument conversion and the export list."""
+"""Host-side behaviour of the public API without a GPU: the Python-side
+error types and messages (fuseop/__init__.py:15-29), argument conversion,
+the fanout and offset checks of the row-sharded entry, and the export list.
+The C++ binding's RuntimeError checks (fuseop/binding.cpp:16-53, :119-135,
+:200-218) are tested on the GPU through the public API
+(tests/test_errors_gpu.py)."""
 
 from __future__ import annotations
 
@@ -85,31 +88,6 @@ def test_python_dtype_checks_raise_type_error(field, value, match):
         fsa._check_python_inputs(g["rowptr"], g["col"], g["x"], g["frontier"])
 
 
-@pytest.mark.parametrize("over,match", [
-    ({"x": FakeCuda(torch.zeros(2, 4), device="cuda:1")}, "same CUDA device"),
-    ({"x": FakeCuda(torch.zeros(8))}, r"expected rowptr\[N\+1\]"),
-    ({"col": FakeCuda(torch.zeros(2, dtype=torch.int32), contiguous=False)}, "contiguous"),
-    ({"rowptr": FakeCuda(torch.tensor([0, 1], dtype=torch.int32))}, "rowptr length must equal N"),
-])
-def test_graph_checks_raise_runtime_error(over, match):
-    g = graph(**over)
-    with pytest.raises(RuntimeError, match=match):
-        fsa._check_graph_inputs(g["rowptr"], g["col"], g["x"], g["frontier"])
-
-
-def test_graph_checks_accept_valid_inputs():
-    g = graph()
-    fsa._check_graph_inputs(g["rowptr"], g["col"], g["x"], g["frontier"])
-
-
-@pytest.mark.parametrize("fanout,match", [(-1, "non-negative"), (1025, "maximum of 1024")])
-def test_fanout_1hop_limits(fanout, match):
-    with pytest.raises(RuntimeError, match=match):
-        fsa._check_fanout_1hop(fanout)
-    fsa._check_fanout_1hop(1024)
-    fsa._check_fanout_1hop(0)
-
-
 @pytest.mark.parametrize("f1,f2,match", [
     (-1, 1, "non-negative"), (1, -1, "non-negative"),
     (2, 2**62, "too large"), (1000, 12, "too much shared memory"),
@@ -135,24 +113,45 @@ def test_int64_conversion():
     assert fsa._as_int64(True, "fanout") == 1
 
 
-def test_backward_shape_checks():
-    s = FakeCuda(torch.zeros(3, 2, dtype=torch.int32))
-    t = FakeCuda(torch.zeros(3, dtype=torch.int32))
-    g = FakeCuda(torch.zeros(4, 5))
-    with pytest.raises(RuntimeError, match="shapes do not match"):
-        fsa._backward_1hop(s, t, g, 10)
-    s1 = FakeCuda(torch.zeros(4, 2, dtype=torch.int32))
-    s2 = FakeCuda(torch.zeros(4, 3, 2, dtype=torch.int32))
-    with pytest.raises(RuntimeError, match="shapes do not match"):
-        fsa._backward_2hop(g, s1, s2, 10)
-    with pytest.raises(RuntimeError, match="invalid backward input dtypes"):
-        fsa._backward_2hop(FakeCuda(torch.zeros(4, 5, dtype=torch.float64)), s1, s1, 10)
-    with pytest.raises(RuntimeError, match="num_nodes must be non-negative"):
-        fsa._backward_1hop(FakeCuda(torch.zeros(4, 2, dtype=torch.int32)),
-                           FakeCuda(torch.zeros(4, dtype=torch.int32)), g, -1)
-
-
 def test_batch_offset_must_be_non_negative():
     with pytest.raises(RuntimeError, match="batch_offset"):
         fsa._check_offset(-1)
     assert fsa._check_offset(5) == 5
+
+
+def test_fuseop_package_serves_this_library():
+    """`import fuseop` (the reference's package name, fuseop/__init__.py:209-214)
+    gives the same four functions as fusesampleagg_b200."""
+    import fuseop
+
+    assert fuseop.__all__ == fsa.__all__
+    for name in fuseop.__all__:
+        assert getattr(fuseop, name) is getattr(fsa, name)
+
+
+def test_bench_module_import_loads_no_library():
+    """bench.py's reference arm must map only the reference's extension: the
+    module itself imports neither this package nor its .so files."""
+    import subprocess
+    import sys
+
+    code = ("import sys, bench; "
+            "assert 'fusesampleagg_b200' not in sys.modules, 'package imported'; "
+            "libs = bench.mapped_repo_libraries(); "
+            "assert not libs, libs")
+    proc = subprocess.run([sys.executable, "-c", code], cwd=str(fsa._lib.LIB_PATH.parents[1]),
+                          capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+
+
+def test_binding_raises_formatted_check_failures():
+    """A TORCH_CHECK failure with a formatted message raised inside the C++
+    binding comes back as RuntimeError, repeatedly (a binding built by a
+    mismatched C++ toolchain crashed the process here instead)."""
+    x = torch.zeros(4, 3)
+    rp = torch.tensor([0, 0, 0, 0, 0], dtype=torch.int32)
+    fr = torch.tensor([0], dtype=torch.int32)
+    for _ in range(50):
+        with pytest.raises(RuntimeError, match=r"grad_buffer shape must equal the features' "
+                                               r"shape \(\[4, 2\] vs \[4, 3\]\)"):
+            fsa._C.sample_agg_2hop_into(rp, rp[:0], x, fr, 2, 2, 1, 0, torch.zeros(4, 2))

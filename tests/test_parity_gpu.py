@@ -288,6 +288,28 @@ def test_non_default_stream(hops):
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("want_ids", [True, False])
+def test_large_batch_resolves_ids_first_and_matches_oracle(want_ids):
+    """32768+ second-hop rows: a flat kernel turns the winners into ids
+    before the gather (plan, scan, draws, resolve, gather), with the ids
+    requested or kept in the workspace."""
+    g = cpu_graph("uniform")
+    rp, cl = dev_graph("uniform")
+    x = cpu_features(g.num_nodes, 12)
+    fr = C.frontier_for("uniform", g, 3000, 10)
+    r1, r2 = oracle.sample_2hop(g.rowptr.numpy(), g.col.numpy(), fr.numpy(), 15, 4, 22)
+    before = fsa.launch_count()
+    if want_ids:
+        out, s1, s2 = fsa.fused_sample_agg_2hop_with_samples(rp, cl, x.cuda(), fr.cuda(), 15, 4,
+                                                             replay_seed=22)
+        np.testing.assert_array_equal(s1.cpu().numpy(), r1)
+        np.testing.assert_array_equal(s2.cpu().numpy(), r2)
+    else:
+        out = fsa.fused_sample_agg_2hop(rp, cl, x.cuda(), fr.cuda(), 15, 4, replay_seed=22)
+    assert fsa.launch_count() == before + 5
+    assert_bit_equal(out, oracle.forward_2hop(x.numpy(), r2))
+
+
 def test_save_indices_without_grad_still_replays():
     g = cpu_graph("toy")
     rp, cl = dev_graph("toy")
@@ -349,6 +371,20 @@ def test_bad_neighbor_and_bad_row_are_flagged():
 # Sort-by-destination backward (alternative to the atomic scatter)
 # ---------------------------------------------------------------------------
 
+def atomic_backward(go, s1, s2, num_nodes, base=None):
+    """The step's backward (red.global.add) through the C ABI, adding into
+    `base` (a copy) or into zeros."""
+    from fusesampleagg_b200 import _lib
+
+    B, D = go.shape
+    grad = (base.clone() if base is not None
+            else torch.zeros((num_nodes, D), device=go.device))
+    _lib.check(_lib.LIB.fsa_sample_agg_2hop_backward(
+        go.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, s1.size(1), s2.size(2),
+        grad.data_ptr(), num_nodes, torch.cuda.current_stream().cuda_stream), "backward")
+    return grad
+
+
 def sorted_backward(go, s1, s2, num_nodes, base=None):
     from fusesampleagg_b200 import _lib
 
@@ -383,7 +419,7 @@ def test_sorted_backward_accumulates_and_matches_atomic_variant():
     go = synthetic.features(s1.size(0), 64, seed=5).cuda()
     base = synthetic.features(g.num_nodes, 64, seed=6).cuda()
     got = sorted_backward(go, s1, s2, g.num_nodes, base=base)
-    want = fsa._backward_2hop(go, s1, s2, g.num_nodes, zeroed=base.clone())
+    want = atomic_backward(go, s1, s2, g.num_nodes, base=base)
     torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
 
 
@@ -395,7 +431,7 @@ def test_sorted_backward_on_c2_graph_matches_atomic_variant():
     _, s1, s2 = fsa.fused_sample_agg_2hop_with_samples(g.rowptr, g.col, x, fr, 15, 10, 3)
     go = synthetic.features(1024, w.dim, seed=2, device="cuda")
     got = sorted_backward(go, s1, s2, g.num_nodes)
-    want = fsa._backward_2hop(go, s1, s2, g.num_nodes)
+    want = atomic_backward(go, s1, s2, g.num_nodes)
     torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
 
 
@@ -472,7 +508,7 @@ def test_2hop_at_the_entry_limit_matches_oracle(fan):
     np.testing.assert_array_equal(s2.cpu().numpy(), r2)
     assert_bit_equal(out, ref_out)
     go = synthetic.features(16, 8, seed=4)
-    grad = fsa._backward_2hop(go.cuda(), s1, s2, g.num_nodes)
+    grad = atomic_backward(go.cuda(), s1, s2, g.num_nodes)
     ref = oracle.backward_2hop(go.numpy(), r1, r2, g.num_nodes)
     np.testing.assert_allclose(grad.cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
 

@@ -35,8 +35,18 @@ def ref():
         "fuseop", REF_DIR / "fuseop" / "__init__.py",
         submodule_search_locations=[str(REF_DIR / "fuseop")])
     mod = importlib.util.module_from_spec(spec)
+    # Registered under its own name only while it imports its _C extension;
+    # afterwards `fuseop` in this process is this repository's package again.
+    prev = sys.modules.get("fuseop")
     sys.modules["fuseop"] = mod
-    spec.loader.exec_module(mod)
+    try:
+        spec.loader.exec_module(mod)
+    finally:
+        sys.modules.pop("fuseop._C", None)
+        if prev is not None:
+            sys.modules["fuseop"] = prev
+        else:
+            del sys.modules["fuseop"]
     return mod
 
 

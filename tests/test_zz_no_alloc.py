@@ -97,19 +97,42 @@ def test_largest_batch_within_scratch():
     assert_same(got[0], want[0])
 
 
+# Stand-in device addresses for the host-side checks below: non-null and
+# aligned, never dereferenced (every call returns before any CUDA call).
+FAKE = 1 << 20
+
+
 def test_oversized_call_is_rejected_before_cuda():
     """Runs without a GPU: the size check precedes every CUDA call."""
     b = 10_000
     assert L.fsa_sample_agg_2hop_workspace_size(b, 15, 10, 1, 1) > _lib.NOALLOC_SCRATCH_BYTES
-    st = L.fsa_sample_agg_2hop_forward_noalloc(None, None, 10, 10, None, 4, None, b, 0, 15, 10,
-                                               1, None, None, None, None, 0, None)
+    st = L.fsa_sample_agg_2hop_forward_noalloc(FAKE, FAKE, 10, 10, FAKE, 4, FAKE, b, 0, 15, 10,
+                                               1, FAKE, None, None, None, 0, None)
     assert st == _lib.FSA_ERR_SCRATCH_LIMIT
     assert b"scratch" in L.fsa_status_string(st)
     # batch sizes far beyond the scratch never reach the layout arithmetic
-    st = L.fsa_sample_agg_2hop_forward_noalloc(None, None, 10, 10, None, 4, None, 1 << 62, 0,
-                                               1, 1, 1, None, None, None, None, 0, None)
+    st = L.fsa_sample_agg_2hop_forward_noalloc(FAKE, FAKE, 10, 10, FAKE, 4, FAKE, 1 << 62, 0,
+                                               1, 1, 1, FAKE, None, None, None, 0, None)
     assert st == _lib.FSA_ERR_SCRATCH_LIMIT
     # no sampling work: no scratch, same result as the workspace entry point
     assert L.fsa_sample_agg_2hop_forward_noalloc(None, None, 10, 10, None, 4, None, 5, 0, 0, 3,
                                                  1, None, None, None, None, 0,
                                                  None) == _lib.FSA_OK
+
+
+@pytest.mark.parametrize("bad", [
+    {"rowptr": None},                   # null graph pointer
+    {"out": None},                      # null output
+    {"offset": -1},                     # negative batch_offset
+    {"zero_count": 8},                  # zero_count > 0 with no zero_fill
+    {"k2": 12000},                      # fanout pair over the entry limit
+])
+def test_oversized_call_with_bad_arguments_is_invalid_argument(bad):
+    """Runs without a GPU: arguments are checked before the size limit, so a
+    call that is both too large and malformed is told it is malformed."""
+    a = {"rowptr": FAKE, "out": FAKE, "offset": 0, "zero_count": 0, "k2": 10}
+    a.update(bad)
+    st = L.fsa_sample_agg_2hop_forward_noalloc(a["rowptr"], FAKE, 10, 10, FAKE, 4, FAKE, 10_000,
+                                               a["offset"], 15, a["k2"], 1, a["out"], None, None,
+                                               None, a["zero_count"], None)
+    assert st == _lib.FSA_ERR_INVALID_ARGUMENT
