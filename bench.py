@@ -247,6 +247,27 @@ class Inputs:
         self.setup_s = time.time() - t0
 
 
+def graph_identical_across_ranks(inp: Inputs, dist: Dist) -> bool | None:
+    """Whether every rank generated the same CSR (None on one GPU): an exact
+    position-weighted int64 sum of rowptr and col (wrapping, so independent
+    of summation order), compared by an all-reduce of its min and max."""
+    if not dist.pg:
+        return None
+    import torch.distributed as tdist
+
+    fp = torch.zeros(2, dtype=torch.int64, device=inp.rowptr.device)
+    for k, t in enumerate((inp.rowptr, inp.col)):
+        step = 1 << 27
+        for s in range(0, t.numel(), step):
+            part = t[s:s + step].to(torch.int64)
+            wgt = torch.arange(s, s + part.numel(), device=part.device) % 1021 + 1
+            fp[k] += (part * wgt).sum()
+    lo, hi = fp.clone(), fp.clone()
+    tdist.all_reduce(lo, op=tdist.ReduceOp.MIN)
+    tdist.all_reduce(hi, op=tdist.ReduceOp.MAX)
+    return bool(torch.equal(lo, hi))
+
+
 def byte_model(w, inp: Inputs, batches: list[int]) -> dict:
     """Algorithmic bytes per batch, per kernel, averaged over `batches`, from
     the samples the op itself draws (independent of the implementation).
@@ -650,6 +671,90 @@ def check_reference_arm_libraries() -> list[str]:
     return libs
 
 
+def persistent_leg(w, inp: Inputs, args, dist: Dist, peak: float) -> dict:
+    """The opt-in persistent gradient (``grad_buffer=PersistentGradient``):
+    the same steps, but each step clears only the rows the previous step's
+    backward touched (fsa_zero_rows_f32 over its saved ids) and the backward
+    adds into the caller's buffer, instead of a fresh dense N x D gradient
+    zero-filled every step.  Device-timed like the main measurement; then one
+    step's buffer is compared with the default path's gradient of the same
+    batch (rtol 1e-5 / atol 1e-6), and the three phases are timed with
+    events (clear, forward without fill, backward)."""
+    import fusesampleagg_b200 as fsa
+
+    k1, k2 = w.fanouts
+    nb = len(inp.frontiers)
+    buf = fsa.PersistentGradient(inp.x)
+
+    def step(i, ev=None):
+        j = i % nb
+        if ev is not None:
+            ev[0].record()
+        buf.zero_()
+        if ev is not None:
+            ev[1].record()
+        out = fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, inp.frontiers[j], k1, k2,
+                                        replay_seed=inp.seeds[j], batch_offset=inp.offset,
+                                        grad_buffer=buf)
+        if ev is not None:
+            ev[2].record()
+        out.backward(inp.grad_out)
+        if ev is not None:
+            ev[3].record()
+
+    launches0 = fsa.launch_count()
+    ms, _ = timed(step, args.steps, args.warmup, dist)
+    launches = (fsa.launch_count() - launches0) * args.steps // (args.steps + args.warmup)
+    # phases, from a shorter pass with events between them
+    n_ev = min(args.steps, 30)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ev)]
+    for i in range(n_ev):
+        step(i, evs[i])
+    torch.cuda.synchronize()
+    ph = [sum(e[k].elapsed_time(e[k + 1]) for e in evs) / n_ev * 1000.0 for k in range(3)]
+    # rows cleared per step: the previous step's saved ids (valid ones)
+    rows = sum(int((ids >= 0).sum()) for ids, _ in buf._touched)
+    clear_bytes = 4.0 * w.dim * rows + 4.0 * k1 * k2 * inp.B
+    # equality with the default path on one batch
+    j = (args.warmup + args.steps) % nb
+    buf.zero_()
+    fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, inp.frontiers[j], k1, k2,
+                              replay_seed=inp.seeds[j], batch_offset=inp.offset,
+                              grad_buffer=buf).backward(inp.grad_out)
+    inp.x.grad = None
+    fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, inp.frontiers[j], k1, k2,
+                              replay_seed=inp.seeds[j], batch_offset=inp.offset
+                              ).backward(inp.grad_out)
+    torch.cuda.synchronize()
+    ok = bool(torch.isclose(buf.grad, inp.x.grad, rtol=1e-5, atol=1e-6).all())
+    inp.x.grad = None
+    del buf
+    torch.cuda.empty_cache()
+    units = w.batch * dist.world * args.steps
+    clear_gbs = clear_bytes / (ph[0] * 1e-6) / 1e9
+    return {
+        "value": units / (ms / 1000.0),
+        "unit": "roots/s",
+        "ms_per_step": ms / args.steps,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "gpu_launches": launches,
+        "phases_us": {"clear_rows": ph[0], "forward_without_fill": ph[1], "backward": ph[2]},
+        "clear_rows_kernel": {
+            "kernel": "fsa_zero_rows_kernel (zero the rows of the previous step's saved ids)",
+            "rows_per_step": rows,
+            "algorithmic_bytes": int(clear_bytes),
+            "achieved_gbs": clear_gbs,
+            "frac_of_measured_hbm": clear_gbs / peak,
+        },
+        "matches_fresh_gradient": ok,
+        "check": ("one step's buffer vs the default path's dense gradient of the same batch, "
+                  "rtol 1e-5 / atol 1e-6"),
+        "api": "fused_sample_agg_2hop(..., grad_buffer=PersistentGradient(x)); buf.zero_() "
+               "before each step",
+    }
+
+
 def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     """The row-sharded mode on the same global batch (2+ GPUs): this rank's
     ids and outputs against the replicated op's for the same slice, bit for
@@ -746,6 +851,7 @@ def c5_leg(args, dist: Dist, dev) -> dict:
     inp = Inputs(w5, dev, dist.rank, dist.world, batches=4)
     setup_s = time.time() - t0
     log(f"[rank {dist.rank}] c5 setup {setup_s:.1f}s graph {inp.stats}")
+    same_graph = graph_identical_across_ranks(inp, dist)
     feats = None
     step_api = api
     if dist.world >= 2:
@@ -767,7 +873,8 @@ def c5_leg(args, dist: Dist, dev) -> dict:
         "warmup": warmup,
         "config": {**w5.describe(), "realized_edges": inp.stats["num_edges"],
                    "realized_max_degree": inp.stats["max_degree"],
-                   "roots_per_gpu": w5.batch, "global_batch": w5.batch * dist.world},
+                   "roots_per_gpu": w5.batch, "global_batch": w5.batch * dist.world,
+                   "graph_identical_across_ranks": same_graph},
         "mode": ("replicated features on one GPU" if feats is None else
                  f"row-sharded features over {dist.world} GPUs (gradient owner-sharded over "
                  "NVLink)"),
@@ -817,6 +924,7 @@ def run(args) -> None:
     batches = args.batches
     inp = Inputs(w, dev, dist.rank, world, batches)
     log(f"[rank {dist.rank}] setup {inp.setup_s:.1f}s graph {inp.stats}")
+    same_graph = graph_identical_across_ranks(inp, dist)
     feats = None
     if args.sharded:
         if args.impl != "ours" or world < 2:
@@ -880,6 +988,7 @@ def run(args) -> None:
             "roots_per_gpu": w.batch,
             "global_batch": w.batch * world,
             "root_batches": batches,
+            "graph_identical_across_ranks": same_graph,
             "parallelism": (f"roots partitioned over {world} GPU(s), graph replicated, "
                             "feature rows and their gradient block-sharded over the GPUs "
                             "(remote rows read and gradient added over NVLink through peer "
@@ -976,6 +1085,8 @@ def run(args) -> None:
         result["unique_leaf_rows_per_batch"] = bytes_model["unique_leaf_rows"]
         result["rng_draws_per_batch"] = bytes_model["rng_draws"]
         result["gpu_launches"] = launches
+        if not args.allreduce_grad:
+            result["persistent_grad"] = persistent_leg(w, inp, args, dist, peak)
         if dist.rank == 0 and world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(w, inp, budget_s=args.cpu_budget)
     else:

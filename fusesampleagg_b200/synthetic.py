@@ -142,7 +142,10 @@ def chung_lu_graph(num_nodes: int, num_edges: int, exponent: float,
     """
     g = _generator(seed, device, "graph")
     w = chung_lu_weights(num_nodes, num_edges, exponent, max_degree, device)
-    cdf = torch.cumsum(w, 0)
+    # The float64 prefix sum runs on the host: a GPU scan's association
+    # order can vary from run to run, which moved a few sampled endpoints
+    # across bin edges and gave ranks of one job slightly different graphs.
+    cdf = torch.cumsum(w.cpu(), 0).to(w.device)
     total = float(cdf[-1])
     perm = torch.randperm(num_nodes, generator=g, device=device).to(torch.int32)
     pairs = int(num_edges * oversample) // 2
