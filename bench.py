@@ -1118,20 +1118,32 @@ def profile_forward(args) -> None:
     followed by its backward; `--profile-forward fused` zeroes the gradient
     inside the forward (the step's configuration), `separate` with the
     stand-alone fill kernel, `none` runs forwards only.  `--backward sorted`
-    runs the sort-by-destination backward instead of the atomic one."""
+    runs the sort-by-destination backward instead of the atomic one.
+    `persistent` runs the persistent-gradient step's kernels: forward without
+    fill, then the rows of the previous call's saved ids zeroed
+    (fsa_zero_rows_f32), then the backward into the same buffer.  `onehop`
+    runs the 1-hop forward (fanout `--fanout`, with saved ids) and its
+    backward into a zeroed gradient on the workload's graph and features."""
     from fusesampleagg_b200 import _lib
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     w = synthetic.WORKLOADS[args.workload]
     inp = Inputs(w, dev, 0, 1, args.calls)
+    if args.profile_forward == "onehop":
+        profile_onehop(args, inp, w)
+        return
     L = _lib.LIB
     k1, k2 = w.fanouts
     B, D, n = inp.B, w.dim, inp.n
     out = torch.empty((B, D), device=dev)
     s1 = torch.empty((B, k1), dtype=torch.int32, device=dev)
     s2 = torch.empty((B, k1, k2), dtype=torch.int32, device=dev)
-    grad = torch.empty((n, D), device=dev) if args.profile_forward != "none" else None
+    grad = None
+    if args.profile_forward != "none":
+        # the persistent buffer starts zeroed once; the others are filled per call
+        grad = (torch.zeros if args.profile_forward == "persistent" else torch.empty)(
+            (n, D), device=dev)
     ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, k1, k2, 1, 1)
     ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
@@ -1139,7 +1151,11 @@ def profile_forward(args) -> None:
     if args.backward == "sorted":
         sws_bytes = L.fsa_sample_agg_2hop_backward_sorted_workspace_size(n, B, k1, k2)
         sws = torch.empty((sws_bytes,), dtype=torch.uint8, device=dev)
+    prev_s2 = None
     for j in range(args.calls):
+        if args.profile_forward == "persistent" and prev_s2 is not None:
+            _lib.check(L.fsa_zero_rows_f32(grad.data_ptr(), n, D, prev_s2.data_ptr(),
+                                           prev_s2.numel(), stream), "zero rows")
         if args.profile_forward == "separate":
             _lib.check(L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fill")
         _lib.check(L.fsa_sample_agg_2hop_forward(
@@ -1155,9 +1171,37 @@ def profile_forward(args) -> None:
             _lib.check(L.fsa_sample_agg_2hop_backward(
                 inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
                 grad.data_ptr(), n, stream), "bwd")
+        prev_s2 = s2.clone()
     torch.cuda.synchronize()
     emit({"profile_forward": args.profile_forward, "calls": args.calls,
           "backward": args.backward, "workload": args.workload})
+
+
+def profile_onehop(args, inp: Inputs, w) -> None:
+    """`--calls` 1-hop forwards (fanout `--fanout`, samples and takes saved)
+    of the workload's root batches through the C ABI, each followed by its
+    backward into a gradient zeroed once up front."""
+    from fusesampleagg_b200 import _lib
+
+    L = _lib.LIB
+    B, D, n, k = inp.B, w.dim, inp.n, args.fanout
+    dev = inp.x.device
+    out = torch.empty((B, D), device=dev)
+    samples = torch.empty((B, k), dtype=torch.int32, device=dev)
+    takes = torch.empty((B,), dtype=torch.int32, device=dev)
+    grad = torch.zeros((n, D), device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    for j in range(args.calls):
+        _lib.check(L.fsa_sample_agg_forward(
+            inp.rowptr.data_ptr(), inp.col.data_ptr(), n, inp.col.numel(), inp.x.data_ptr(), D,
+            inp.frontiers[j].data_ptr(), B, 0, k, inp.seeds[j], out.data_ptr(),
+            samples.data_ptr(), takes.data_ptr(), stream), "1-hop fwd")
+        _lib.check(L.fsa_sample_agg_backward(
+            samples.data_ptr(), takes.data_ptr(), inp.grad_out.data_ptr(), B, D, k,
+            grad.data_ptr(), n, stream), "1-hop bwd")
+    torch.cuda.synchronize()
+    emit({"profile_forward": "onehop", "calls": args.calls, "fanout": k,
+          "workload": args.workload})
 
 
 def main() -> None:
@@ -1185,9 +1229,11 @@ def main() -> None:
     p.add_argument("--allreduce-grad", action="store_true",
                    help="replicated features: all-reduce the dense feature gradient after "
                         "every backward (NCCL)")
-    p.add_argument("--profile-forward", choices=["fused", "separate", "none"],
+    p.add_argument("--profile-forward",
+                   choices=["fused", "separate", "none", "persistent", "onehop"],
                    help="run a short C-ABI call sequence for ncu instead of the benchmark")
     p.add_argument("--calls", type=int, default=3, help="calls of --profile-forward")
+    p.add_argument("--fanout", type=int, default=10, help="fanout of --profile-forward onehop")
     p.add_argument("--backward", choices=["atomic", "sorted"], default="atomic",
                    help="backward variant of --profile-forward")
     args = p.parse_args()

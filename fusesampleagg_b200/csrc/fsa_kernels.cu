@@ -55,6 +55,8 @@ __device__ constexpr JumpTables g_jump = fsa::make_jump_tables();
 __device__ unsigned int g_status;
 
 constexpr int kThreads1Hop = 128;
+// Leaf rows a 1-hop forward thread has in flight (then summed in slot order).
+constexpr int kBatch1Hop = 4;
 constexpr int kThreadsBwd = 256;
 constexpr int kThreadsFill = 256;
 // Float4 stores per thread of the zero fill.  A flat grid of short CTAs that
@@ -292,7 +294,7 @@ struct Fwd1Args {
 };
 
 template <int V>
-__global__ void __launch_bounds__(kThreads1Hop)
+__global__ void __launch_bounds__(kThreads1Hop, 8)
     fsa_1hop_forward_kernel(const Fwd1Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* slots = reinterpret_cast<int*>(smem_raw);  // winners, then sample ids
@@ -334,14 +336,26 @@ __global__ void __launch_bounds__(kThreads1Hop)
     for (int64_t v = tid; v < dvec; v += nthreads) {
       VecF<V> acc;
       vzero(acc);
-      for (int i = 0; i < take; ++i) {
-        const int32_t leaf = slots[i];
-        if (leaf >= 0 && leaf < a.num_nodes) {
-          const VecF<V> r = load_stream<V>(a.x + static_cast<int64_t>(leaf) * a.feature_dim + v * V);
+      // kBatch1Hop rows in flight per thread, then summed in slot order.
+      for (int i0 = 0; i0 < take; i0 += kBatch1Hop) {
+        VecF<V> rows[kBatch1Hop];
+        bool ok[kBatch1Hop];
 #pragma unroll
-          for (int c = 0; c < V; ++c) acc.v[c] += r.v[c];
-        } else if (v == 0) {
-          flag_status(FSA_STATUS_BAD_NEIGHBOR);
+        for (int u = 0; u < kBatch1Hop; ++u) {
+          const int32_t leaf = i0 + u < take ? slots[i0 + u] : -1;
+          ok[u] = leaf >= 0 && leaf < a.num_nodes;
+          if (ok[u]) {
+            rows[u] = load_stream<V>(a.x + static_cast<int64_t>(leaf) * a.feature_dim + v * V);
+          } else if (i0 + u < take && v == 0) {
+            flag_status(FSA_STATUS_BAD_NEIGHBOR);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch1Hop; ++u) {
+          if (ok[u]) {
+#pragma unroll
+            for (int c = 0; c < V; ++c) acc.v[c] += rows[u].v[c];
+          }
         }
       }
       if (take > 0) {
@@ -390,7 +404,18 @@ __device__ __forceinline__ void wait_prerequisites() {
 constexpr int kThreadsPlan = 128;
 constexpr int kThreadsScan = 1024;
 constexpr int kThreadsDraw = 768;
-constexpr int kThreadsGather = 256;
+// Gather CTA sizes: roots whose (slot, feature-vector) items fit
+// kGatherSmallItems run on kThreadsGatherSmall threads (8 CTAs per SM at 64
+// registers: 1,184 roots resident at once, so a 1,024-root batch runs in one
+// wave); wider rows, tiled in shared memory, on kThreadsGatherWide.
+// Measured gather times (us; fraction of measured HBM copy bandwidth):
+// 1,024 roots, 15 x 10, D = 100: 256 threads 24.7 (0.33), 128 threads 20.6
+// (0.40), 96 22.2, 64 26.2; 4,096 roots, D = 128: 72.3 -> 67.4; 65,536
+// roots, D = 128: 944 -> 824 (0.81); D = 602 (rows tiled): 256 threads
+// 139.6, 128 threads 159.9.
+constexpr int kThreadsGatherSmall = 128;
+constexpr int kThreadsGatherWide = 256;
+constexpr int kGatherSmallItems = 512;
 
 // Draws of a second-hop row are split into chunks of kChunk positions; the
 // chunks of all rows are numbered consecutively (roots in batch order, their
@@ -848,7 +873,6 @@ struct Gather2Args {
   int32_t* samples2;     // optional id output; may alias win2
   float* out;
   int dchunk;            // feature tile width (multiple of the vector width)
-  int ids_ready;         // win2 already holds the ids (fsa_2hop_resolve_kernel ran)
   RowShards xs;          // sharded feature rows (kSharded kernels only)
 };
 
@@ -879,8 +903,8 @@ constexpr int kGatherBatch = 10;
 // that kGatherBatch rows are in flight per thread) and divides by the valid
 // count; then the slot means are summed in slot order and divided by the
 // non-empty count (fused_sample_agg.cu:189-213).
-template <int V, bool kSharded>
-__global__ void __launch_bounds__(kThreadsGather, 4)
+template <int V, bool kSharded, int kThreads>
+__global__ void __launch_bounds__(kThreads, 1024 / kThreads)
     fsa_2hop_gather_kernel(const Gather2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int k1 = a.fanout1;
@@ -907,9 +931,7 @@ __global__ void __launch_bounds__(kThreadsGather, 4)
       const int j = e - i * k2;
       const int64_t r = b * k1 + i;
       int32_t id = -1;
-      if (a.ids_ready) {
-        id = a.win2[b * k12 + e];
-      } else if (j < __ldg(a.mtake + r)) {
+      if (j < __ldg(a.mtake + r)) {
         const int w = a.win2[b * k12 + e];
         id = __ldg(a.col + static_cast<int64_t>(__ldg(a.mbeg + r)) + (w >= 0 ? w : j));
       }
@@ -984,49 +1006,6 @@ __global__ void __launch_bounds__(kThreadsGather, 4)
       __syncthreads();
     }
     __syncthreads();
-  }
-}
-
-// Winners -> second-hop ids for every (root, slot, j) of the batch, one
-// thread per entry, written over the winner (win2 is samples2 when the
-// caller asked for ids, else workspace).  Slot j of a row holds col[winner],
-// or col[j] if no draw replaced it -- the serial loop's final reservoir
-// (fused_sample_agg.cu:40-56); -1 past the row's take.  Used for large
-// batches (kResolveMinRows second-hop rows and up): resolving all ids in one
-// flat pass takes the dependent col lookups out of every root's chain in the
-// gather kernel that follows (measured, 65,536 roots at 15 x 10 with
-// D = 128: gather 994 -> 942 us including this kernel).  For small batches
-// the extra launch costs more than it saves (1024 roots: 24.7 -> 25.7 us),
-// and the gather resolves the ids itself.
-struct Resolve2Args {
-  const int32_t* col;
-  int64_t num_nodes;
-  int64_t entries;  // batch_size * fanout1 * fanout2
-  int fanout2;
-  const int32_t* mbeg;   // [B*k1]
-  const int32_t* mtake;  // [B*k1]
-  int32_t* win2;         // [B][k1][k2] winners in, ids out
-};
-
-constexpr int kThreadsResolve = 256;
-constexpr int64_t kResolveMinRows = 32768;
-
-__global__ void __launch_bounds__(kThreadsResolve) fsa_2hop_resolve_kernel(const Resolve2Args a) {
-  // A programmatic dependent of the draw kernel: the winners are its results.
-  wait_prerequisites();
-  launch_dependents();
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < a.entries;
-       e += stride) {
-    const int64_t r = e / a.fanout2;
-    const int j = static_cast<int>(e - r * a.fanout2);
-    int32_t id = -1;
-    if (j < __ldg(a.mtake + r)) {
-      const int w = a.win2[e];
-      id = __ldg(a.col + static_cast<int64_t>(__ldg(a.mbeg + r)) + (w >= 0 ? w : j));
-      if (id >= a.num_nodes) flag_status(FSA_STATUS_BAD_NEIGHBOR);
-    }
-    a.win2[e] = id;
   }
 }
 
@@ -1327,10 +1306,12 @@ __global__ void __launch_bounds__(kThreadsFill)
 }
 
 // Zeroes table rows rows[k] (0 <= rows[k] < num_rows; others, such as the -1
-// padding of saved ids, are skipped): one warp per listed row, V-float
-// stores.  Plain (L2-allocating) stores: the rows are about to receive the
-// backward's red.add, which then hits L2.  A row listed twice is written
-// twice with the same zeros.
+// padding of saved ids, are skipped).  A warp takes 32 consecutive list
+// entries with one coalesced load, then stores each listed row in turn
+// (V-float stores by its lanes), so the stores of 32 rows issue back to back
+// behind a single id load.  Plain (L2-allocating) stores: the rows are about
+// to receive the backward's red.add, which then hits L2.  A row listed twice
+// is written twice with the same zeros.
 template <int V>
 __global__ void __launch_bounds__(kThreadsFill)
     fsa_zero_rows_kernel(float* __restrict__ table, int64_t num_rows, int64_t dim,
@@ -1340,12 +1321,15 @@ __global__ void __launch_bounds__(kThreadsFill)
   const int64_t dvec = dim / V;
   VecF<V> z;
   vzero(z);
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       e < count; e += warps) {
-    const int32_t r = __ldg(rows + e);
-    if (r < 0 || r >= num_rows) continue;
-    float* p = table + static_cast<int64_t>(r) * dim;
-    for (int64_t v = lane; v < dvec; v += 32) store_vec(p + v * V, z);
+  for (int64_t t0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
+       t0 < count; t0 += warps * 32) {
+    const int32_t mine = t0 + lane < count ? __ldg(rows + t0 + lane) : -1;
+    for (int u = 0; u < 32; ++u) {
+      const int32_t r = __shfl_sync(0xffffffffU, mine, u);
+      if (r < 0 || r >= num_rows) continue;  // the same for every lane
+      float* p = table + static_cast<int64_t>(r) * dim;
+      for (int64_t v = lane; v < dvec; v += 32) store_vec(p + v * V, z);
+    }
   }
 }
 
@@ -1513,6 +1497,24 @@ bool plan_gather(int k1, int k2, int64_t D, int vec, int* dchunk_out, int* smem_
   *dchunk_out = dchunk;
   *smem_out = l.total;
   return l.total <= kMaxSmemBytes;
+}
+
+// The gather kernel for vector width V: the small- or wide-CTA instance, on
+// a shard table (plain launch) or as a programmatic dependent of the kernel
+// before it.
+template <int V>
+int launch_gather(bool sharded, bool small, int grid, int threads, int smem, cudaStream_t s,
+                  const Gather2Args& ga) {
+  if (sharded) {
+    return small ? launch(fsa_2hop_gather_kernel<V, true, kThreadsGatherSmall>, grid, threads,
+                          smem, s, ga)
+                 : launch(fsa_2hop_gather_kernel<V, true, kThreadsGatherWide>, grid, threads,
+                          smem, s, ga);
+  }
+  return small ? launch_dependent(fsa_2hop_gather_kernel<V, false, kThreadsGatherSmall>, grid,
+                                  threads, smem, s, ga)
+               : launch_dependent(fsa_2hop_gather_kernel<V, false, kThreadsGatherWide>, grid,
+                                  threads, smem, s, ga);
 }
 
 // Persistent grid of the draw kernel.
@@ -1717,32 +1719,16 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
   if (st == FSA_OK) st = pe.mark(3, s);
   if (st != FSA_OK) return st;
   Gather2Args ga{col, x, num_nodes, feature_dim, batch_size, fanout1, fanout2, mbeg,
-                 mtake, win2, samples2, out, dchunk, 0, RowShards{}};
+                 mtake, win2, samples2, out, dchunk, RowShards{}};
   if (xs != nullptr) ga.xs = *xs;
-  if (batch_size * fanout1 >= kResolveMinRows) {
-    // winners -> ids in place (win2 is samples2 when ids were requested)
-    const int64_t entries = batch_size * fanout1 * fanout2;
-    const Resolve2Args ra{col, num_nodes, entries, fanout2, mbeg, mtake, win2};
-    st = launch_dependent(fsa_2hop_resolve_kernel,
-                          grid_for((entries + kThreadsResolve - 1) / kThreadsResolve),
-                          kThreadsResolve, 0, s, ra);
-    if (st != FSA_OK) return st;
-    ga.samples2 = nullptr;  // the ids are already in place
-    ga.ids_ready = 1;
-  }
   const int ggrid = grid_for(batch_size);
-  if (xs != nullptr) {
-    switch (vec) {
-      case 4: st = launch(fsa_2hop_gather_kernel<4, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
-      case 2: st = launch(fsa_2hop_gather_kernel<2, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
-      default: st = launch(fsa_2hop_gather_kernel<1, true>, ggrid, kThreadsGather, gsmem, s, ga); break;
-    }
-  } else {
-    switch (vec) {
-      case 4: st = launch_dependent(fsa_2hop_gather_kernel<4, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
-      case 2: st = launch_dependent(fsa_2hop_gather_kernel<2, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
-      default: st = launch_dependent(fsa_2hop_gather_kernel<1, false>, ggrid, kThreadsGather, gsmem, s, ga); break;
-    }
+  const bool small = static_cast<int64_t>(fanout1) * (dchunk / vec) <= kGatherSmallItems;
+  const int threads = small ? kThreadsGatherSmall : kThreadsGatherWide;
+  const bool sh = xs != nullptr;
+  switch (vec) {
+    case 4: st = launch_gather<4>(sh, small, ggrid, threads, gsmem, s, ga); break;
+    case 2: st = launch_gather<2>(sh, small, ggrid, threads, gsmem, s, ga); break;
+    default: st = launch_gather<1>(sh, small, ggrid, threads, gsmem, s, ga); break;
   }
   if (st == FSA_OK) st = pe.mark(4, s);
   return st;
@@ -1980,7 +1966,7 @@ int fsa_zero_rows_f32(float* table, int64_t num_rows, int64_t dim, const int32_t
   if (count == 0 || num_rows == 0 || dim == 0) return FSA_OK;
   auto s = static_cast<cudaStream_t>(stream);
   const int vec = pick_vec(dim, table, table);
-  const int64_t per_cta = kThreadsFill / 32;
+  const int64_t per_cta = kThreadsFill;  // 32 list entries per warp
   const int grid = grid_for((count + per_cta - 1) / per_cta);
   switch (vec) {
     case 4: fsa_zero_rows_kernel<4><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;

@@ -288,28 +288,6 @@ def test_non_default_stream(hops):
     assert torch.equal(out, ref)
 
 
-@pytest.mark.parametrize("want_ids", [True, False])
-def test_large_batch_resolves_ids_first_and_matches_oracle(want_ids):
-    """32768+ second-hop rows: a flat kernel turns the winners into ids
-    before the gather (plan, scan, draws, resolve, gather), with the ids
-    requested or kept in the workspace."""
-    g = cpu_graph("uniform")
-    rp, cl = dev_graph("uniform")
-    x = cpu_features(g.num_nodes, 12)
-    fr = C.frontier_for("uniform", g, 3000, 10)
-    r1, r2 = oracle.sample_2hop(g.rowptr.numpy(), g.col.numpy(), fr.numpy(), 15, 4, 22)
-    before = fsa.launch_count()
-    if want_ids:
-        out, s1, s2 = fsa.fused_sample_agg_2hop_with_samples(rp, cl, x.cuda(), fr.cuda(), 15, 4,
-                                                             replay_seed=22)
-        np.testing.assert_array_equal(s1.cpu().numpy(), r1)
-        np.testing.assert_array_equal(s2.cpu().numpy(), r2)
-    else:
-        out = fsa.fused_sample_agg_2hop(rp, cl, x.cuda(), fr.cuda(), 15, 4, replay_seed=22)
-    assert fsa.launch_count() == before + 5
-    assert_bit_equal(out, oracle.forward_2hop(x.numpy(), r2))
-
-
 def test_save_indices_without_grad_still_replays():
     g = cpu_graph("toy")
     rp, cl = dev_graph("toy")
