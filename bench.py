@@ -74,10 +74,10 @@ NOMINAL_HBM_GBS = 8000.0
 NCU_TRAFFIC = {
     "c2_2hop_powerlaw": {
         "draw": 1.09e6 + 919.0e6,
-        "gather": 56.0e6 + 0.05e6,
-        "plan": 1.86e6,
+        "gather": 55.53e6 + 0.62e6,
+        "plan": 1.88e6,
         "scan": 0.02e6,
-        "bwd": 42.65e6 + 2.38e6,
+        "bwd": 42.32e6 + 3.25e6,
     },
 }
 

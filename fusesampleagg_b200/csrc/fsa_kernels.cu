@@ -1309,26 +1309,43 @@ __global__ void __launch_bounds__(kThreadsFill)
 // padding of saved ids, are skipped).  A warp takes 32 consecutive list
 // entries with one coalesced load, then stores each listed row in turn
 // (V-float stores by its lanes), so the stores of 32 rows issue back to back
-// behind a single id load.  Plain (L2-allocating) stores: the rows are about
-// to receive the backward's red.add, which then hits L2.  A row listed twice
-// is written twice with the same zeros.
-template <int V>
+// behind a single id load.  kOneStore: rows of at most 32 vectors, one
+// predicated store per lane and row (about six instructions a row; the
+// general loop cost about forty and bound the kernel by instruction issue).
+// Plain (L2-allocating) stores: the rows are about to receive the
+// backward's red.add, which then hits L2.  A row listed twice is written
+// twice with the same zeros.
+template <int V, bool kOneStore>
 __global__ void __launch_bounds__(kThreadsFill)
     fsa_zero_rows_kernel(float* __restrict__ table, int64_t num_rows, int64_t dim,
                          const int32_t* __restrict__ rows, int64_t count) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t dvec = dim / V;
+  // ids are int32, so the range check is one unsigned compare
+  const uint32_t nrows = num_rows < 0x7fffffffLL ? static_cast<uint32_t>(num_rows) : 0x7fffffffU;
   VecF<V> z;
   vzero(z);
+  float* lane_base = table + static_cast<int64_t>(lane) * V;
+  const bool lane_on = lane < dvec;
   for (int64_t t0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
        t0 < count; t0 += warps * 32) {
     const int32_t mine = t0 + lane < count ? __ldg(rows + t0 + lane) : -1;
-    for (int u = 0; u < 32; ++u) {
-      const int32_t r = __shfl_sync(0xffffffffU, mine, u);
-      if (r < 0 || r >= num_rows) continue;  // the same for every lane
-      float* p = table + static_cast<int64_t>(r) * dim;
-      for (int64_t v = lane; v < dvec; v += 32) store_vec(p + v * V, z);
+    if (kOneStore) {
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int32_t r = __shfl_sync(0xffffffffU, mine, u);
+        if (static_cast<uint32_t>(r) < nrows && lane_on) {
+          store_vec(lane_base + static_cast<int64_t>(r) * dim, z);
+        }
+      }
+    } else {
+      for (int u = 0; u < 32; ++u) {
+        const int32_t r = __shfl_sync(0xffffffffU, mine, u);
+        if (static_cast<uint32_t>(r) >= nrows) continue;  // the same for every lane
+        float* p = table + static_cast<int64_t>(r) * dim;
+        for (int64_t v = lane; v < dvec; v += 32) store_vec(p + v * V, z);
+      }
     }
   }
 }
@@ -1968,10 +1985,14 @@ int fsa_zero_rows_f32(float* table, int64_t num_rows, int64_t dim, const int32_t
   const int vec = pick_vec(dim, table, table);
   const int64_t per_cta = kThreadsFill;  // 32 list entries per warp
   const int grid = grid_for((count + per_cta - 1) / per_cta);
-  switch (vec) {
-    case 4: fsa_zero_rows_kernel<4><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
-    case 2: fsa_zero_rows_kernel<2><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
-    default: fsa_zero_rows_kernel<1><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+  const bool one = dim / vec <= 32;
+  switch (vec * 2 + (one ? 1 : 0)) {
+    case 9: fsa_zero_rows_kernel<4, true><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+    case 8: fsa_zero_rows_kernel<4, false><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+    case 5: fsa_zero_rows_kernel<2, true><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+    case 4: fsa_zero_rows_kernel<2, false><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+    case 3: fsa_zero_rows_kernel<1, true><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
+    default: fsa_zero_rows_kernel<1, false><<<grid, kThreadsFill, 0, s>>>(table, num_rows, dim, rows, count); break;
   }
   return check_launch();
 }
