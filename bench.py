@@ -570,6 +570,29 @@ def kernel_times(w, inp: Inputs, iters: int) -> dict:
         torch.cuda.synchronize()
         res["fill_alone"] += ev[0].elapsed_time(ev[1])
         res["fwd_nofill"] += ev[1].elapsed_time(ev[2])
+    # The backward after a forward without the fused fill (no dirty fill
+    # lines draining from L2 while it runs), and the row clear of the
+    # persistent gradient (the rows of one step's saved ids) launched
+    # back to back, so that no host gap falls between the events.
+    res["bwd_after_nofill"] = 0.0
+    for it in range(iters):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        fwd(it % nb, False)
+        ev[0].record()
+        bwd()
+        ev[1].record()
+        torch.cuda.synchronize()
+        res["bwd_after_nofill"] += ev[0].elapsed_time(ev[1])
+    reps = 20
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    fwd(0, False)
+    ev[0].record()
+    for _ in range(reps):
+        _lib.check(L.fsa_zero_rows_f32(grad.data_ptr(), n, D, s2.data_ptr(), s2.numel(), stream),
+                   "zero rows")
+    ev[1].record()
+    torch.cuda.synchronize()
+    res["zero_rows"] = ev[0].elapsed_time(ev[1]) * iters / reps
     times = {k: 1000.0 * v / calls for k, v in phases.items()}
     times.update({k: 1000.0 * v / iters for k, v in res.items()})
     return times
@@ -671,15 +694,16 @@ def check_reference_arm_libraries() -> list[str]:
     return libs
 
 
-def persistent_leg(w, inp: Inputs, args, dist: Dist, peak: float) -> dict:
+def persistent_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     """The opt-in persistent gradient (``grad_buffer=PersistentGradient``):
-    the same steps, but each step clears only the rows the previous step's
-    backward touched (fsa_zero_rows_f32 over its saved ids) and the backward
-    adds into the caller's buffer, instead of a fresh dense N x D gradient
+    the same steps, but each step's forward clears only the rows the previous
+    step's backward touched (``clear_grad_buffer=True``: zeroed inside the
+    sampling kernel from the previous step's saved ids) and the backward adds
+    into the caller's buffer, instead of a fresh dense N x D gradient
     zero-filled every step.  Device-timed like the main measurement; then one
     step's buffer is compared with the default path's gradient of the same
-    batch (rtol 1e-5 / atol 1e-6), and the three phases are timed with
-    events (clear, forward without fill, backward)."""
+    batch (rtol 1e-5 / atol 1e-6), and the forward and backward are timed
+    with events."""
     import fusesampleagg_b200 as fsa
 
     k1, k2 = w.fanouts
@@ -690,37 +714,25 @@ def persistent_leg(w, inp: Inputs, args, dist: Dist, peak: float) -> dict:
         j = i % nb
         if ev is not None:
             ev[0].record()
-        buf.zero_()
-        if ev is not None:
-            ev[1].record()
         out = fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, inp.frontiers[j], k1, k2,
                                         replay_seed=inp.seeds[j], batch_offset=inp.offset,
-                                        grad_buffer=buf)
+                                        grad_buffer=buf, clear_grad_buffer=True)
         if ev is not None:
-            ev[2].record()
+            ev[1].record()
         out.backward(inp.grad_out)
         if ev is not None:
-            ev[3].record()
+            ev[2].record()
 
     launches0 = fsa.launch_count()
+    ms, phases = timed(step, args.steps, args.warmup, dist, phase_events=True)
     ms, _ = timed(step, args.steps, args.warmup, dist)
-    launches = (fsa.launch_count() - launches0) * args.steps // (args.steps + args.warmup)
-    # phases, from a shorter pass with events between them
-    n_ev = min(args.steps, 30)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ev)]
-    for i in range(n_ev):
-        step(i, evs[i])
-    torch.cuda.synchronize()
-    ph = [sum(e[k].elapsed_time(e[k + 1]) for e in evs) / n_ev * 1000.0 for k in range(3)]
-    # rows cleared per step: the previous step's saved ids (valid ones)
+    launches = (fsa.launch_count() - launches0) * args.steps // (2 * (args.steps + args.warmup))
     rows = sum(int((ids >= 0).sum()) for ids, _ in buf._touched)
-    clear_bytes = 4.0 * w.dim * rows + 4.0 * k1 * k2 * inp.B
     # equality with the default path on one batch
     j = (args.warmup + args.steps) % nb
-    buf.zero_()
     fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, inp.frontiers[j], k1, k2,
                               replay_seed=inp.seeds[j], batch_offset=inp.offset,
-                              grad_buffer=buf).backward(inp.grad_out)
+                              grad_buffer=buf, clear_grad_buffer=True).backward(inp.grad_out)
     inp.x.grad = None
     fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, inp.x, inp.frontiers[j], k1, k2,
                               replay_seed=inp.seeds[j], batch_offset=inp.offset
@@ -731,7 +743,6 @@ def persistent_leg(w, inp: Inputs, args, dist: Dist, peak: float) -> dict:
     del buf
     torch.cuda.empty_cache()
     units = w.batch * dist.world * args.steps
-    clear_gbs = clear_bytes / (ph[0] * 1e-6) / 1e9
     return {
         "value": units / (ms / 1000.0),
         "unit": "roots/s",
@@ -739,19 +750,15 @@ def persistent_leg(w, inp: Inputs, args, dist: Dist, peak: float) -> dict:
         "steps": args.steps,
         "warmup": args.warmup,
         "gpu_launches": launches,
-        "phases_us": {"clear_rows": ph[0], "forward_without_fill": ph[1], "backward": ph[2]},
-        "clear_rows_kernel": {
-            "kernel": "fsa_zero_rows_kernel (zero the rows of the previous step's saved ids)",
-            "rows_per_step": rows,
-            "algorithmic_bytes": int(clear_bytes),
-            "achieved_gbs": clear_gbs,
-            "frac_of_measured_hbm": clear_gbs / peak,
-        },
+        "phases_ms": phases,
+        "rows_cleared_per_step": rows,
+        "clear": ("rows of the previous step's saved ids zeroed by the draw kernel's two "
+                  "fill warps (fsa_sample_agg_2hop_forward_zero_rows), no kernel of its own"),
         "matches_fresh_gradient": ok,
         "check": ("one step's buffer vs the default path's dense gradient of the same batch, "
                   "rtol 1e-5 / atol 1e-6"),
-        "api": "fused_sample_agg_2hop(..., grad_buffer=PersistentGradient(x)); buf.zero_() "
-               "before each step",
+        "api": "fused_sample_agg_2hop(..., grad_buffer=PersistentGradient(x), "
+               "clear_grad_buffer=True)",
     }
 
 
@@ -1048,6 +1055,18 @@ def run(args) -> None:
         kernels["draw"]["rng_draws_per_launch"] = bytes_model["rng_draws"]
         kernels["draw"]["rng_draws_per_s"] = bytes_model["rng_draws"] / (kt["draw"] * 1e-6)
         kernels["forward_without_fill_us"] = kt["fwd_nofill"]
+        kernels["bwd_after_forward_without_fill_us"] = kt["bwd_after_nofill"]
+        rows_bytes = (4.0 * w.dim * bytes_model["valid_leaves"]
+                      + 4.0 * inp.B * w.fanouts[0] * w.fanouts[1])
+        kernels["zero_rows"] = {
+            "kernel": "fsa_zero_rows_kernel (stand-alone clear of one step's saved-id rows, "
+                      "as PersistentGradient.zero_() runs it; 20 launches back to back; the "
+                      "persistent step clears inside the draw kernel instead)",
+            "avg_us": kt["zero_rows"],
+            "algorithmic_bytes": int(rows_bytes),
+            "achieved_gbs": rows_bytes / (kt["zero_rows"] * 1e-6) / 1e9,
+            "frac_of_measured_hbm": rows_bytes / (kt["zero_rows"] * 1e-6) / 1e9 / peak,
+        }
         kernels["bwd_sorted_alternative"] = {
             "kernels": "fsa_2hop_sortbwd_{count,scatter,reduce}_kernel + fsa_sortbwd_scan_"
                        "{tiles,totals}_kernel + counts zero fill (sort-by-destination "
@@ -1086,7 +1105,7 @@ def run(args) -> None:
         result["rng_draws_per_batch"] = bytes_model["rng_draws"]
         result["gpu_launches"] = launches
         if not args.allreduce_grad:
-            result["persistent_grad"] = persistent_leg(w, inp, args, dist, peak)
+            result["persistent_grad"] = persistent_leg(w, inp, args, dist)
         if dist.rank == 0 and world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(w, inp, budget_s=args.cpu_budget)
     else:
@@ -1119,9 +1138,10 @@ def profile_forward(args) -> None:
     inside the forward (the step's configuration), `separate` with the
     stand-alone fill kernel, `none` runs forwards only.  `--backward sorted`
     runs the sort-by-destination backward instead of the atomic one.
-    `persistent` runs the persistent-gradient step's kernels: forward without
-    fill, then the rows of the previous call's saved ids zeroed
-    (fsa_zero_rows_f32), then the backward into the same buffer.  `onehop`
+    `persistent` runs the persistent-gradient step's kernels: the forward
+    that zeroes the rows of the previous call's saved ids inside its draw
+    kernel (fsa_sample_agg_2hop_forward_zero_rows), then the backward into
+    the same buffer.  `onehop`
     runs the 1-hop forward (fanout `--fanout`, with saved ids) and its
     backward into a zeroed gradient on the workload's graph and features."""
     from fusesampleagg_b200 import _lib
@@ -1153,9 +1173,19 @@ def profile_forward(args) -> None:
         sws = torch.empty((sws_bytes,), dtype=torch.uint8, device=dev)
     prev_s2 = None
     for j in range(args.calls):
-        if args.profile_forward == "persistent" and prev_s2 is not None:
-            _lib.check(L.fsa_zero_rows_f32(grad.data_ptr(), n, D, prev_s2.data_ptr(),
-                                           prev_s2.numel(), stream), "zero rows")
+        if args.profile_forward == "persistent":
+            # the previous call's rows zeroed inside this call's draw kernel
+            _lib.check(L.fsa_sample_agg_2hop_forward_zero_rows(
+                inp.rowptr.data_ptr(), inp.col.data_ptr(), n, inp.col.numel(), inp.x.data_ptr(),
+                D, inp.frontiers[j].data_ptr(), B, 0, k1, k2, inp.seeds[j], out.data_ptr(),
+                s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, grad.data_ptr(),
+                prev_s2.data_ptr() if prev_s2 is not None else None,
+                prev_s2.numel() if prev_s2 is not None else 0, stream), "fwd zero rows")
+            _lib.check(L.fsa_sample_agg_2hop_backward(
+                inp.grad_out.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1, k2,
+                grad.data_ptr(), n, stream), "bwd")
+            prev_s2 = s2.clone()
+            continue
         if args.profile_forward == "separate":
             _lib.check(L.fsa_fill_zero_f32(grad.data_ptr(), grad.numel(), stream), "fill")
         _lib.check(L.fsa_sample_agg_2hop_forward(

@@ -142,15 +142,19 @@ def _ptr(t):
 # ---------------------------------------------------------------------------
 
 def fused_sample_agg(rowptr, col, x, frontier, fanout, replay_seed=1234, save_indices=False,
-                     *, batch_offset=0, grad_buffer=None):
+                     *, batch_offset=0, grad_buffer=None, clear_grad_buffer=False):
     """Return the sampled 1-hop neighbor mean for each frontier node."""
     _check_python_inputs(rowptr, col, x, frontier)
     fanout = _as_int64(fanout, "fanout")
     seed = _as_seed(replay_seed)
     offset = _as_int64(batch_offset, "batch_offset")
+    if clear_grad_buffer and grad_buffer is None:
+        raise ValueError("clear_grad_buffer needs a grad_buffer")
     if grad_buffer is not None:
-        out, ids, flag = _C.sample_agg_into(rowptr, col, x, frontier, fanout, seed, offset,
-                                            _buffer_tensor(grad_buffer))
+        buf = _buffer_tensor(grad_buffer)
+        if clear_grad_buffer:
+            grad_buffer.zero_()
+        out, ids, flag = _C.sample_agg_into(rowptr, col, x, frontier, fanout, seed, offset, buf)
         grad_buffer._record(ids, flag)
         return out
     return _C.sample_agg(rowptr, col, x, frontier, fanout, seed, bool(save_indices), offset)
@@ -170,16 +174,29 @@ def fused_sample_agg_with_samples(rowptr, col, x, frontier, fanout, replay_seed=
 
 
 def fused_sample_agg_2hop(rowptr, col, x, frontier, fanout1, fanout2, replay_seed=1234,
-                          save_indices=False, *, batch_offset=0, grad_buffer=None):
-    """Return the nested sampled 2-hop neighbor mean for each frontier node."""
+                          save_indices=False, *, batch_offset=0, grad_buffer=None,
+                          clear_grad_buffer=False):
+    """Return the nested sampled 2-hop neighbor mean for each frontier node.
+
+    ``clear_grad_buffer=True`` (with a ``grad_buffer``) does what
+    ``grad_buffer.zero_()`` right before the call would, inside the call:
+    the rows are zeroed by the sampling kernel, whose draws leave the memory
+    system idle, instead of by a kernel of their own.
+    """
     _check_python_inputs(rowptr, col, x, frontier)
     f1 = _as_int64(fanout1, "fanout1")
     f2 = _as_int64(fanout2, "fanout2")
     seed = _as_seed(replay_seed)
     offset = _as_int64(batch_offset, "batch_offset")
+    if clear_grad_buffer and grad_buffer is None:
+        raise ValueError("clear_grad_buffer needs a grad_buffer")
     if grad_buffer is not None:
+        buf = _buffer_tensor(grad_buffer)
+        rows = grad_buffer._rows_to_clear() if clear_grad_buffer else None
         out, ids, flag = _C.sample_agg_2hop_into(rowptr, col, x, frontier, f1, f2, seed, offset,
-                                                 _buffer_tensor(grad_buffer))
+                                                 buf, rows)
+        if clear_grad_buffer:
+            grad_buffer._cleared()
         grad_buffer._record(ids, flag)
         return out
     return _C.sample_agg_2hop(rowptr, col, x, frontier, f1, f2, seed, bool(save_indices),
@@ -248,16 +265,28 @@ class PersistentGradient:
 
     def zero_(self) -> "PersistentGradient":
         """Zeroes the rows touched since the last call (one fsa_zero_rows_f32
-        launch per recorded call)."""
-        keep = []
-        for ids, flag in self._touched:
-            _C.zero_rows(self.grad, ids)
-            # still awaiting its backward, and its graph (which holds the
-            # other reference to the flag) is alive
-            if int(flag[0]) != 0 and flag._use_count() > 1:
-                keep.append((ids, flag))
-        self._touched = keep
+        launch over the recorded calls' saved ids)."""
+        rows = self._rows_to_clear()
+        if rows is not None:
+            _C.zero_rows(self.grad, rows)
+        self._cleared()
         return self
+
+    def _rows_to_clear(self):
+        """The recorded calls' saved ids as one int32 list, or None."""
+        if not self._touched:
+            return None
+        if len(self._touched) == 1:
+            return self._touched[0][0].reshape(-1)
+        return torch.cat([ids.reshape(-1) for ids, _ in self._touched])
+
+    def _cleared(self) -> None:
+        """Forgets the recorded calls whose rows were just zeroed, except
+        those still awaiting their backward (their rows will be touched
+        again): still pending, and their graph -- which holds the other
+        reference to the flag -- is alive."""
+        self._touched = [(ids, flag) for ids, flag in self._touched
+                         if int(flag[0]) != 0 and flag._use_count() > 1]
 
 
 def _buffer_tensor(buf) -> torch.Tensor:

@@ -42,6 +42,9 @@ SIGNATURES = {
     "fsa_sample_agg_2hop_forward": (
         _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p,
                _p, ctypes.c_size_t, _p, _i64, _p]),
+    "fsa_sample_agg_2hop_forward_zero_rows": (
+        _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p,
+               _p, ctypes.c_size_t, _p, _p, _i64, _p]),
     "fsa_sample_agg_2hop_forward_noalloc": (
         _int, [_p, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _u64, _p, _p, _p,
                _p, _i64, _p]),

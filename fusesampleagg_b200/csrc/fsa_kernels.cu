@@ -623,6 +623,13 @@ struct Draw2Args {
   float4* fill;                      // optional buffer to zero (16-byte aligned)
   int64_t fill_vec4;                 // float4 elements of `fill`
   int smem_roots;                    // rpre staged in shared memory when B < this
+  // optional rows to zero instead (fill_vec4 == 0): rows zrows[k] of ztable,
+  // zdim4 (<= 32) float4 each, ids outside [0, znum_rows) skipped
+  float4* ztable;
+  const int32_t* zrows;
+  int64_t zrows_count;
+  int zdim4;
+  uint32_t znum_rows;
 };
 
 // Fill work item: 32 KB (kFillItemVec4 float4 stores per lane of a warp).
@@ -682,6 +689,24 @@ __device__ __forceinline__ void fill_items_bulk(unsigned long long* counter, lon
     issued = true;
   }
   if (issued) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Zeroes the rows named by list entries [32 item, 32 item + 32): one
+// coalesced id load, then one float4 store per lane and row (rows of at most
+// 32 float4).  All 32 lanes must call it.
+__device__ __forceinline__ void zero_row_tile(const Draw2Args& a, long long item, int lane) {
+  const long long e = item * 32 + lane;
+  const int32_t mine = e < a.zrows_count ? __ldg(a.zrows + e) : -1;
+  const float4 z = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+  float4* base = a.ztable + lane;
+  const bool on = lane < a.zdim4;
+#pragma unroll
+  for (int u = 0; u < 32; ++u) {
+    const int32_t r = __shfl_sync(0xffffffffU, mine, u);
+    if (static_cast<uint32_t>(r) < a.znum_rows && on) {
+      base[static_cast<int64_t>(r) * a.zdim4] = z;
+    }
+  }
 }
 
 // Claims the next work item of counter `c` for the warp (lane 0 adds, the
@@ -795,7 +820,27 @@ __global__ void __launch_bounds__(kThreadsDraw, 2) fsa_2hop_draw_kernel(const Dr
   __syncthreads();
   const int warps = static_cast<int>(blockDim.x >> 5);
   const int warp = static_cast<int>(threadIdx.x >> 5);
-  const int fillers = a.fill_vec4 > 0 ? kFillWarps : 0;
+  // Row mode: zero listed rows (the rows a persistent gradient buffer's
+  // previous backwards touched) instead of a whole buffer.  Both filler
+  // warps store; the items are tiles of 32 list entries.
+  const bool rows_mode = a.fill_vec4 == 0 && a.zrows_count > 0;
+  const int fillers = (a.fill_vec4 > 0 || rows_mode) ? kFillWarps : 0;
+  if (warp < fillers && rows_mode) {
+    const long long nitems = (a.zrows_count + 31) / 32;
+    const long long share = nitems * kFillStaticNum / kFillStaticDen / gridDim.x;
+    const long long share0 = static_cast<long long>(blockIdx.x) * share;
+    const long long dyn0 = static_cast<long long>(gridDim.x) * share;
+    for (long long item = share0 + claim(&s_fill_next, lane); item < share0 + share;
+         item = share0 + claim(&s_fill_next, lane)) {
+      zero_row_tile(a, item, lane);
+    }
+    wait_prerequisites();
+    for (long long item = dyn0 + claim(a.next, lane); item < nitems;
+         item = dyn0 + claim(a.next, lane)) {
+      zero_row_tile(a, item, lane);
+    }
+    return;
+  }
   if (warp < fillers) {
     const long long nfill = (a.fill_vec4 + 32LL * kFillItemVec4 - 1) / (32LL * kFillItemVec4);
     const long long share = nfill * kFillStaticNum / kFillStaticDen / gridDim.x;
@@ -1662,7 +1707,8 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
                         int32_t fanout1, int32_t fanout2, uint64_t seed, float* out,
                         int32_t* samples1, int32_t* samples2, void* workspace,
                         size_t workspace_bytes, float* zero_fill, int64_t zero_count,
-                        void* stream, const RowShards* xs) {
+                        void* stream, const RowShards* xs, float* zero_table = nullptr,
+                        const int32_t* zero_rows = nullptr, int64_t zero_rows_count = 0) {
   const int arg_status =
       check_forward_2hop_args(rowptr, col, num_nodes, num_edges, x, feature_dim, frontier,
                               batch_size, batch_offset, fanout1, fanout2, out, zero_fill,
@@ -1673,6 +1719,23 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
                             samples2 == nullptr);
   if (work && (workspace == nullptr || workspace_bytes < wl.total || !aligned(workspace, 256))) {
     return FSA_ERR_INVALID_ARGUMENT;
+  }
+  // Listed rows of a [num_nodes][feature_dim] table to zero (the row-sparse
+  // counterpart of zero_fill): in the draw kernel when the rows are whole
+  // float4 vectors (at most 32 of them) and no dense fill rides along, else
+  // with the stand-alone row kernel before the forward.
+  float4* ztable4 = nullptr;
+  if (zero_rows_count > 0) {
+    const bool fuse = work && zero_count == 0 && feature_dim % 4 == 0 &&
+                      feature_dim / 4 <= 32 && aligned(zero_table, 16) &&
+                      num_nodes <= 0x7fffffffLL;
+    if (fuse) {
+      ztable4 = reinterpret_cast<float4*>(zero_table);
+    } else {
+      const int st0 = fsa_zero_rows_f32(zero_table, num_nodes, feature_dim, zero_rows,
+                                        zero_rows_count, stream);
+      if (st0 != FSA_OK) return st0;
+    }
   }
   // The zero fill rides along in the draw kernel (float4 stores); a buffer
   // that is not 16-byte aligned or has a count % 4 tail, or a call with no
@@ -1730,7 +1793,10 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
   st = draw_grid(&dgrid);
   if (st != FSA_OK) return st;
   const Draw2Args da{rgroups, rpre, lpre, state, mtake, mdraws, batch_size, fanout1, fanout2,
-                     win2, next, fill4, fill_vec4, kSmemRoots};
+                     win2, next, fill4, fill_vec4, kSmemRoots, ztable4,
+                     ztable4 != nullptr ? zero_rows : nullptr,
+                     ztable4 != nullptr ? zero_rows_count : 0,
+                     static_cast<int>(feature_dim / 4), static_cast<uint32_t>(num_nodes)};
   const int dsmem = kDrawTableBytes + kRprePad + (fill_vec4 > 0 ? kZeroBytes : 0);
   st = launch_dependent(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st == FSA_OK) st = pe.mark(3, s);
@@ -1764,6 +1830,26 @@ int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* col,
   return forward_2hop(rowptr, col, num_nodes, num_edges, x, feature_dim, frontier, batch_size,
                       batch_offset, fanout1, fanout2, seed, out, samples1, samples2, workspace,
                       workspace_bytes, zero_fill, zero_count, stream, nullptr);
+}
+
+int fsa_sample_agg_2hop_forward_zero_rows(const int32_t* rowptr, const int32_t* col,
+                                          int64_t num_nodes, int64_t num_edges,
+                                          const float* x, int64_t feature_dim,
+                                          const int32_t* frontier, int64_t batch_size,
+                                          int64_t batch_offset, int32_t fanout1,
+                                          int32_t fanout2, uint64_t seed, float* out,
+                                          int32_t* samples1, int32_t* samples2,
+                                          void* workspace, size_t workspace_bytes,
+                                          float* zero_table, const int32_t* zero_rows,
+                                          int64_t zero_rows_count, void* stream) {
+  if (zero_rows_count < 0 || (zero_rows_count > 0 && zero_rows == nullptr) ||
+      (zero_rows_count > 0 && num_nodes > 0 && feature_dim > 0 && zero_table == nullptr)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  return forward_2hop(rowptr, col, num_nodes, num_edges, x, feature_dim, frontier, batch_size,
+                      batch_offset, fanout1, fanout2, seed, out, samples1, samples2, workspace,
+                      workspace_bytes, nullptr, 0, stream, nullptr, zero_table, zero_rows,
+                      zero_rows_count);
 }
 
 // Shard table from a host array of device pointers; checks the count, the

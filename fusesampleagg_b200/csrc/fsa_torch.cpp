@@ -215,7 +215,9 @@ std::tuple<Tensor, Tensor, Tensor> forward_2hop(const Tensor& rowptr_in, const T
                                                 const Tensor& x_in, const Tensor& frontier_in,
                                                 int64_t f1, int64_t f2, uint64_t seed,
                                                 bool capture, int64_t batch_offset,
-                                                const Tensor& zero) {
+                                                const Tensor& zero,
+                                                const Tensor& clear_table = Tensor(),
+                                                const Tensor& clear_rows = Tensor()) {
   const Tensor rowptr = rowptr_in.contiguous();
   const Tensor col = col_in.contiguous();
   const Tensor x = x_in.contiguous();
@@ -228,8 +230,15 @@ std::tuple<Tensor, Tensor, Tensor> forward_2hop(const Tensor& rowptr_in, const T
   const c10::cuda::CUDAGuard guard(x.device());
   auto f32 = x.options();
   auto i32 = x.options().dtype(at::kInt);
+  const bool clearing = clear_rows.defined() && clear_rows.numel() > 0;
   if (B == 0 || f1 == 0 || f2 == 0) {
     if (zero.defined()) zero.zero_();
+    if (clearing) {
+      check_status(fsa_zero_rows_f32(clear_table.data_ptr<float>(), clear_table.size(0),
+                                     clear_table.size(1), clear_rows.data_ptr<int32_t>(),
+                                     clear_rows.numel(), stream_of(x)),
+                   "fsa_zero_rows_f32");
+    }
     return {at::zeros({B, D}, f32), at::full({B, f1}, -1, i32), at::full({B, f1, f2}, -1, i32)};
   }
   const size_t ws_bytes = fsa_sample_agg_2hop_workspace_size(
@@ -249,6 +258,18 @@ std::tuple<Tensor, Tensor, Tensor> forward_2hop(const Tensor& rowptr_in, const T
   } else {
     ws = at::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(at::kByte));
     ws_ptr = ws.data_ptr();
+  }
+  if (clearing) {
+    check_status(fsa_sample_agg_2hop_forward_zero_rows(
+                     rowptr.data_ptr<int32_t>(), col.data_ptr<int32_t>(), x.size(0),
+                     col.numel(), x.data_ptr<float>(), D, frontier.data_ptr<int32_t>(), B,
+                     batch_offset, static_cast<int32_t>(f1), static_cast<int32_t>(f2), seed,
+                     out.data_ptr<float>(), capture ? s1.data_ptr<int32_t>() : nullptr,
+                     capture ? s2.data_ptr<int32_t>() : nullptr, ws_ptr, ws_bytes,
+                     clear_table.data_ptr<float>(), clear_rows.data_ptr<int32_t>(),
+                     clear_rows.numel(), stream_of(x)),
+                 "fsa_sample_agg_2hop_forward_zero_rows");
+    return {out, s1, s2};
   }
   check_status(fsa_sample_agg_2hop_forward(
                    rowptr.data_ptr<int32_t>(), col.data_ptr<int32_t>(), x.size(0), col.numel(),
@@ -421,9 +442,10 @@ Tensor pending_flag() { return at::ones({1}, at::TensorOptions().dtype(at::kInt)
 struct SampleAgg2HopInto : public torch::autograd::Function<SampleAgg2HopInto> {
   static variable_list forward(AutogradContext* ctx, const Tensor& rowptr, const Tensor& col,
                                const Tensor& x, const Tensor& frontier, int64_t f1, int64_t f2,
-                               uint64_t seed, int64_t batch_offset, const Tensor& into) {
-    auto [out, s1, s2] =
-        forward_2hop(rowptr, col, x, frontier, f1, f2, seed, true, batch_offset, Tensor());
+                               uint64_t seed, int64_t batch_offset, const Tensor& into,
+                               const Tensor& clear_rows) {
+    auto [out, s1, s2] = forward_2hop(rowptr, col, x, frontier, f1, f2, seed, true,
+                                      batch_offset, Tensor(), into, clear_rows);
     Tensor flag = pending_flag();
     ctx->save_for_backward({s1, s2});
     ctx->saved_data["into"] = into;
@@ -447,20 +469,34 @@ struct SampleAgg2HopInto : public torch::autograd::Function<SampleAgg2HopInto> {
                    "fsa_sample_agg_2hop_backward");
     }
     ctx->saved_data["flag"].toTensor().data_ptr<int32_t>()[0] = 0;
-    return variable_list(9);
+    return variable_list(10);
   }
 };
 
+// `clear_rows` (optional): saved ids whose rows of `into` are zeroed as part
+// of this call (inside the sampling kernel when the row width allows).
 std::vector<Tensor> sample_agg_2hop_into(const Tensor& rowptr, const Tensor& col,
                                          const Tensor& x, const Tensor& frontier, int64_t f1,
                                          int64_t f2, uint64_t seed, int64_t batch_offset,
-                                         const Tensor& into) {
+                                         const Tensor& into,
+                                         const c10::optional<Tensor>& clear_rows) {
   check_grad_into(into, x);
+  // an empty list rather than an undefined tensor: autograd's apply needs a
+  // device for every tensor argument
+  Tensor rows = at::empty({0}, into.options().dtype(at::kInt));
+  if (clear_rows.has_value() && clear_rows->defined()) {
+    rows = *clear_rows;
+    TORCH_CHECK(rows.is_cuda() && rows.device() == into.device() &&
+                    rows.scalar_type() == at::kInt && rows.is_contiguous(),
+                "clear_rows must be contiguous int32 on the buffer's device");
+  }
   if (!(at::GradMode::is_enabled() && x.requires_grad())) {
-    auto r = forward_2hop(rowptr, col, x, frontier, f1, f2, seed, false, batch_offset, Tensor());
+    auto r = forward_2hop(rowptr, col, x, frontier, f1, f2, seed, false, batch_offset, Tensor(),
+                          into, rows);
     return {std::get<0>(r), Tensor(), Tensor()};
   }
-  return SampleAgg2HopInto::apply(rowptr, col, x, frontier, f1, f2, seed, batch_offset, into);
+  return SampleAgg2HopInto::apply(rowptr, col, x, frontier, f1, f2, seed, batch_offset, into,
+                                  rows);
 }
 
 struct SampleAgg1HopInto : public torch::autograd::Function<SampleAgg1HopInto> {

@@ -128,6 +128,33 @@ FSA_API int fsa_sample_agg_2hop_forward(const int32_t* rowptr, const int32_t* co
                                         void* stream);
 
 /*
+ * The 2-hop forward that also zeroes listed rows of a table -- the
+ * row-sparse counterpart of zero_fill above, for a feature gradient kept
+ * across steps (no counterpart in the reference, whose backward zero-fills a
+ * fresh N x D gradient every call, fuseop/binding.cpp:137, :220).  Same
+ * arguments and results as fsa_sample_agg_2hop_forward, with zero_fill /
+ * zero_count replaced by zero_table float32[num_nodes][feature_dim] and the
+ * row list zero_rows int32[zero_rows_count] (typically the samples2 of the
+ * previous steps; entries outside [0, num_nodes) such as -1 padding are
+ * skipped).  The rows are zero when the call's work on `stream` has
+ * finished.  When feature_dim is a multiple of 4 (at most 128) and
+ * zero_table is 16-byte aligned, the rows are zeroed inside the sampling
+ * kernel, whose draws leave the memory system idle; otherwise
+ * fsa_zero_rows_f32 runs first.  zero_table must not be read by this call's
+ * forward (it is the gradient, not x).
+ */
+FSA_API int fsa_sample_agg_2hop_forward_zero_rows(const int32_t* rowptr, const int32_t* col,
+                                                  int64_t num_nodes, int64_t num_edges,
+                                                  const float* x, int64_t feature_dim,
+                                                  const int32_t* frontier, int64_t batch_size,
+                                                  int64_t batch_offset, int32_t fanout1,
+                                                  int32_t fanout2, uint64_t seed, float* out,
+                                                  int32_t* samples1, int32_t* samples2,
+                                                  void* workspace, size_t workspace_bytes,
+                                                  float* zero_table, const int32_t* zero_rows,
+                                                  int64_t zero_rows_count, void* stream);
+
+/*
  * 2-hop forward on library-owned scratch.  No counterpart in the reference:
  * the reference launcher (fuseop/fused_sample_agg.cu:303-315) needs no
  * scratch, and the workspace entry point above takes it from the caller.

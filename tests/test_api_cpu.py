@@ -154,4 +154,4 @@ def test_binding_raises_formatted_check_failures():
     for _ in range(50):
         with pytest.raises(RuntimeError, match=r"grad_buffer shape must equal the features' "
                                                r"shape \(\[4, 2\] vs \[4, 3\]\)"):
-            fsa._C.sample_agg_2hop_into(rp, rp[:0], x, fr, 2, 2, 1, 0, torch.zeros(4, 2))
+            fsa._C.sample_agg_2hop_into(rp, rp[:0], x, fr, 2, 2, 1, 0, torch.zeros(4, 2), None)

@@ -215,3 +215,80 @@ def test_persistent_gradient_argument_checks(graph):
         fsa.fused_sample_agg_2hop(rp, cl, x, fr, 2, 2, grad_buffer=other)
     with pytest.raises(ValueError, match="2-D CUDA feature tensor"):
         fsa.PersistentGradient(x.detach().cpu())
+
+
+@pytest.mark.parametrize("hops", [1, 2])
+def test_clear_inside_the_call_equals_zero_then_call(graph, hops):
+    """clear_grad_buffer=True: the recorded rows are zeroed as part of the
+    call (for 2-hop inside the sampling kernel); every step's buffer equals
+    the default path's fresh gradient."""
+    rp, cl, n = graph
+    D = 100
+    x = synthetic.features(n, D, seed=1, device="cuda").requires_grad_(True)
+    buf = fsa.PersistentGradient(x)
+    for step in range(4):
+        fr = roots(n, 1024, 300 + step)
+        go = synthetic.features(1024, D, seed=400 + step, device="cuda")
+        torch.cuda.synchronize()
+        launches = fsa.launch_count()
+        if hops == 2:
+            out = fsa.fused_sample_agg_2hop(rp, cl, x, fr, 15, 10, replay_seed=step,
+                                            grad_buffer=buf, clear_grad_buffer=True)
+        else:
+            out = fsa.fused_sample_agg(rp, cl, x, fr, 10, replay_seed=step, grad_buffer=buf,
+                                       clear_grad_buffer=True)
+        out.backward(go)
+        torch.cuda.synchronize()
+        if hops == 2:
+            # plan, draw (with the row clear), gather, backward
+            assert fsa.launch_count() - launches == 4
+        want = (fresh_grad_2hop(rp, cl, x, fr, go, step) if hops == 2
+                else fresh_grad_1hop(rp, cl, x, fr, go, step))
+        torch.testing.assert_close(buf.grad, want, rtol=RTOL, atol=ATOL)
+    with pytest.raises(ValueError, match="needs a grad_buffer"):
+        fsa.fused_sample_agg_2hop(rp, cl, x, roots(n, 8, 1), 2, 2, clear_grad_buffer=True)
+
+
+@pytest.mark.parametrize("dim", [100, 37, 256])
+def test_forward_zero_rows_entry_point(graph, dim):
+    """fsa_sample_agg_2hop_forward_zero_rows through the C ABI: the listed rows
+    (with -1 padding and out-of-range entries) of the table are zero, all
+    other rows unchanged, and the forward's outputs are those of the plain
+    entry point.  D = 100 clears inside the draw kernel; D = 37 and 256 take
+    the stand-alone row kernel first."""
+    from fusesampleagg_b200 import _lib
+
+    L = _lib.LIB
+    rp, cl, n = graph
+    x = synthetic.features(n, dim, seed=1, device="cuda")
+    fr = roots(n, 512, 7)
+    B, k1, k2 = 512, 15, 10
+    table = torch.ones((n, dim), device="cuda")
+    rows = torch.randint(0, n, (3000,), dtype=torch.int32, device="cuda")
+    rows[::7] = -1
+    rows[::11] = n + 5
+    stream = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for clear in (False, True):
+        out = torch.empty((B, dim), device="cuda")
+        s1 = torch.empty((B, k1), dtype=torch.int32, device="cuda")
+        s2 = torch.empty((B, k1, k2), dtype=torch.int32, device="cuda")
+        nbytes = L.fsa_sample_agg_2hop_workspace_size(B, k1, k2, 1, 1)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        head = (rp.data_ptr(), cl.data_ptr(), n, cl.numel(), x.data_ptr(), dim, fr.data_ptr(), B,
+                0, k1, k2, 9, out.data_ptr(), s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), nbytes)
+        if clear:
+            st = L.fsa_sample_agg_2hop_forward_zero_rows(*head, table.data_ptr(), rows.data_ptr(),
+                                                         rows.numel(), stream)
+        else:
+            st = L.fsa_sample_agg_2hop_forward(*head, None, 0, stream)
+        _lib.check(st, "2-hop forward")
+        outs.append((out, s1, s2))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0].view(torch.int32), outs[1][0].view(torch.int32))
+    assert torch.equal(outs[0][2], outs[1][2])
+    valid = rows[(rows >= 0) & (rows < n)].long()
+    mask = torch.zeros(n, dtype=torch.bool, device="cuda")
+    mask[valid] = True
+    assert torch.count_nonzero(table[mask]) == 0
+    assert bool((table[~mask] == 1).all())
