@@ -412,10 +412,13 @@ constexpr int kThreadsDraw = 768;
 // 1,024 roots, 15 x 10, D = 100: 256 threads 24.7 (0.33), 128 threads 20.6
 // (0.40), 96 22.2, 64 26.2; 4,096 roots, D = 128: 72.3 -> 67.4; 65,536
 // roots, D = 128: 944 -> 824 (0.81); D = 602 (rows tiled): 256 threads
-// 139.6, 128 threads 159.9.
+// 139.6, 128 threads 159.9.  With no more roots than the wide CTAs hold at
+// once the small CTA only adds item rounds (512 roots, 8 x 4, D = 200:
+// 128 threads 14.7, 256 threads 12.6), so it is used only above that.
 constexpr int kThreadsGatherSmall = 128;
 constexpr int kThreadsGatherWide = 256;
 constexpr int kGatherSmallItems = 512;
+constexpr int kGatherWidePerSm = 1024 / kThreadsGatherWide;  // resident wide CTAs per SM
 
 // Draws of a second-hop row are split into chunks of kChunk positions; the
 // chunks of all rows are numbered consecutively (roots in batch order, their
@@ -1579,6 +1582,24 @@ int launch_gather(bool sharded, bool small, int grid, int threads, int smem, cud
                                   threads, smem, s, ga);
 }
 
+// Number of SMs of the current device (cached per device).
+int sm_count(int* out) {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) {
+    *out = cached[dev];
+    return FSA_OK;
+  }
+  int sms = 0;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (dev >= 0 && dev < 64) cached[dev] = sms;
+  *out = sms;
+  return FSA_OK;
+}
+
 // Persistent grid of the draw kernel.
 int draw_grid(int* grid_out) {
   static int cached[64] = {0};
@@ -1805,7 +1826,13 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
                  mtake, win2, samples2, out, dchunk, RowShards{}};
   if (xs != nullptr) ga.xs = *xs;
   const int ggrid = grid_for(batch_size);
-  const bool small = static_cast<int64_t>(fanout1) * (dchunk / vec) <= kGatherSmallItems;
+  // The small CTA only pays when the wide one would not hold every root at
+  // once (4 wide CTAs per SM); with fewer roots it only adds item rounds.
+  int sms = 0;
+  st = sm_count(&sms);
+  if (st != FSA_OK) return st;
+  const bool small = static_cast<int64_t>(fanout1) * (dchunk / vec) <= kGatherSmallItems &&
+                     batch_size > static_cast<int64_t>(sms) * kGatherWidePerSm;
   const int threads = small ? kThreadsGatherSmall : kThreadsGatherWide;
   const bool sh = xs != nullptr;
   switch (vec) {
