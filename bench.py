@@ -583,6 +583,23 @@ def kernel_times(w, inp: Inputs, iters: int) -> dict:
         ev[1].record()
         torch.cuda.synchronize()
         res["bwd_after_nofill"] += ev[0].elapsed_time(ev[1])
+    # The backward after the forward and a 256 MB read, which writes the
+    # dirty lines the forward left in L2 back to HBM before the backward
+    # starts; against "bwd", the share of the backward's live time that is
+    # the forward's write-back.
+    res["bwd_after_writeback"] = 0.0
+    flush = torch.ones(64 << 20, device=dev)
+    acc = torch.zeros(1, device=dev)
+    for it in range(iters):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        fwd(it % nb, True)
+        torch.sum(flush, dim=0, keepdim=True, out=acc)
+        ev[0].record()
+        bwd()
+        ev[1].record()
+        torch.cuda.synchronize()
+        res["bwd_after_writeback"] += ev[0].elapsed_time(ev[1])
+    del flush, acc
     reps = 20
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     fwd(0, False)
@@ -1056,6 +1073,7 @@ def run(args) -> None:
         kernels["draw"]["rng_draws_per_s"] = bytes_model["rng_draws"] / (kt["draw"] * 1e-6)
         kernels["forward_without_fill_us"] = kt["fwd_nofill"]
         kernels["bwd_after_forward_without_fill_us"] = kt["bwd_after_nofill"]
+        kernels["bwd_after_forward_writeback_us"] = kt["bwd_after_writeback"]
         rows_bytes = (4.0 * w.dim * bytes_model["valid_leaves"]
                       + 4.0 * inp.B * w.fanouts[0] * w.fanouts[1])
         kernels["zero_rows"] = {

@@ -1115,38 +1115,62 @@ struct Bwd2Args {
   int64_t num_nodes;
 };
 
-// One CTA per root; items are (first-hop slot, feature vector) pairs.
+// Slot stride of the backward's shared leaf ids: k2 rounded up to 4, so a
+// slot's ids start 16-byte aligned and an item reads them four at a time.
+__host__ __device__ inline int bwd_slot_stride(int k2) { return (k2 + 3) & ~3; }
+
+// One CTA per root; items are (first-hop slot, feature vector) pairs.  One
+// pass puts the root's leaf ids in shared memory (padded with -1 to the slot
+// stride) and counts each slot's valid ids with shared-memory atomics as they
+// arrive; a first-hop id of -1 marks its slot empty (fused_sample_agg.cu:
+// 229-240: a slot is non-empty when its first-hop id is valid and it has a
+// valid second-hop id).  After one barrier every warp counts the non-empty
+// slots with ballots.  The counts alternate between two arrays by root, so
+// the next root's counting needs no extra barrier to clear them.
 template <int V, bool kSharded>
-__global__ void __launch_bounds__(kThreadsBwd)
+__global__ void __launch_bounds__(kThreadsBwd, 8)
     fsa_2hop_backward_kernel(const Bwd2Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int k1 = a.fanout1;
   const int k2 = a.fanout2;
   const int k12 = k1 * k2;
-  int* valid = reinterpret_cast<int*>(smem_raw);  // [k1]
-  int* s2 = valid + k1;                            // [k1 * k2]
-  int* misc = s2 + k12;                            // [1]
+  const int k2p = bwd_slot_stride(k2);
+  int* s2 = reinterpret_cast<int*>(smem_raw);  // [k1][k2p] leaf ids, -1 padded
+  int* valid2 = s2 + k1 * k2p;                 // [2][k1] valid counts, by root parity
+  int* mid_ok = valid2 + 2 * k1;               // [k1] first-hop id present
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
+  const int lane = tid & 31;
   const int64_t dvec = a.feature_dim / V;
+  for (int i = tid; i < 2 * k1; i += nthreads) valid2[i] = 0;
   // May be launched as a programmatic dependent of the kernel before it:
   // wait for that grid before reading anything.
   wait_prerequisites();
+  __syncthreads();
 
-  for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
-    if (tid == 0) misc[0] = 0;
-    for (int e = tid; e < k12; e += nthreads) s2[e] = a.samples2[b * k12 + e];
-    __syncthreads();
-    for (int i = tid; i < k1; i += nthreads) {
-      int cnt = 0;
-      for (int j = 0; j < k2; ++j) cnt += s2[i * k2 + j] >= 0 ? 1 : 0;
-      valid[i] = cnt;
-      // fused_sample_agg.cu:229-240: a slot is non-empty when its first-hop id
-      // is valid and it has at least one valid second-hop id.
-      if (cnt > 0 && a.samples1[b * k1 + i] >= 0) atomicAdd(&misc[0], 1);
+  int parity = 0;
+  for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x, parity ^= 1) {
+    int* valid = valid2 + parity * k1;
+    int* other = valid2 + (parity ^ 1) * k1;
+    for (int i = tid; i < k1; i += nthreads) other[i] = 0;  // the next root's counts
+    for (int e = tid; e < k12; e += nthreads) {
+      const int i = e / k2;
+      const int j = e - i * k2;
+      const int32_t leaf = a.samples2[b * k12 + e];
+      s2[i * k2p + j] = leaf;
+      if (leaf >= 0) atomicAdd(&valid[i], 1);
+      if (j == 0) mid_ok[i] = a.samples1[b * k1 + i] >= 0 ? 1 : 0;
+    }
+    for (int e = tid; e < k1 * (k2p - k2); e += nthreads) {
+      const int i = e / (k2p - k2);
+      s2[i * k2p + k2 + (e - i * (k2p - k2))] = -1;
     }
     __syncthreads();
-    const int nonempty = misc[0];
+    int nonempty = 0;
+    for (int i0 = 0; i0 < k1; i0 += 32) {
+      const int i = i0 + lane;
+      nonempty += __popc(__ballot_sync(0xffffffffU, i < k1 && valid[i] > 0 && mid_ok[i] != 0));
+    }
     if (nonempty > 0) {
       const float ne = static_cast<float>(nonempty);
       const int64_t items = static_cast<int64_t>(k1) * dvec;
@@ -1159,16 +1183,23 @@ __global__ void __launch_bounds__(kThreadsBwd)
         const float vc = static_cast<float>(cnt);
 #pragma unroll
         for (int c = 0; c < V; ++c) g.v[c] = (g.v[c] / ne) / vc;
-        const int32_t* leaves = s2 + i * k2;
-        for (int j = 0; j < k2; ++j) {
-          const int32_t leaf = leaves[j];
-          if (leaf < 0) continue;
-          if (leaf < a.num_nodes) {
-            red_add<V>(kSharded ? shard_row(a.gs, leaf, a.feature_dim) + v * V
-                                : a.grad_x + static_cast<int64_t>(leaf) * a.feature_dim + v * V,
-                       g);
-          } else if (v == 0) {
-            flag_status(FSA_STATUS_BAD_NEIGHBOR);
+        const int4* leaves = reinterpret_cast<const int4*>(s2 + i * k2p);
+#pragma unroll 1
+        for (int j4 = 0; j4 < k2p / 4; ++j4) {
+          const int4 q = leaves[j4];
+          const int32_t lv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int32_t leaf = lv[u];
+            if (leaf < 0) continue;
+            if (leaf < a.num_nodes) {
+              red_add<V>(kSharded ? shard_row(a.gs, leaf, a.feature_dim) + v * V
+                                  : a.grad_x + static_cast<int64_t>(leaf) * a.feature_dim +
+                                        v * V,
+                         g);
+            } else if (v == 0) {
+              flag_status(FSA_STATUS_BAD_NEIGHBOR);
+            }
           }
         }
       }
@@ -1940,7 +1971,7 @@ static int backward_2hop(const float* grad_out, const int32_t* samples1,
   Bwd2Args a{RowShards{}, grad_out, samples1, samples2, batch_size, feature_dim,
              fanout1, fanout2, grad_x, num_nodes};
   const int vec = pick_vec(feature_dim, grad_out, grad_x);
-  const int smem = 4 * (fanout1 + fanout1 * fanout2 + 1);
+  const int smem = 4 * (fanout1 * bwd_slot_stride(fanout2) + 3 * fanout1);
   const int grid = grid_for(batch_size);
   auto s = static_cast<cudaStream_t>(stream);
   if (gs != nullptr) {

@@ -474,7 +474,7 @@ def test_gradient_accumulates_over_two_backwards():
 # Fanouts at the shared-memory limit (f1 + f1 * f2 <= 12000)
 # ---------------------------------------------------------------------------
 
-@pytest.mark.parametrize("fan", [(5, 2399), (1, 11999), (109, 109)])
+@pytest.mark.parametrize("fan", [(5, 2399), (1, 11999), (109, 109), (5999, 1)])
 def test_2hop_at_the_entry_limit_matches_oracle(fan):
     # hub graph: root 9 links to rows 0 (60,000 neighbours), 8 (20,000), 6
     # and 7 (1024 / 1025), so second-hop rows draw far past the fanout
