@@ -20,11 +20,15 @@ rewritten every step, so inputs exceed the 126 MB L2 between steps.
 Multi-GPU (torchrun): one process per GPU, graph and features replicated,
 each rank takes its contiguous 1024-root slice of a global batch with
 ``batch_offset = rank * 1024`` (ids identical to a single-GPU run of the
-global batch); no collective on the data path (weak scaling).
+global batch); no collective on the data path (weak scaling).  After the
+main measurement, on 2+ GPUs: the same step followed by the NCCL all-reduce
+of the dense feature gradient (`replicated_allreduce`), the row-sharded mode
+checked bit for bit against the replicated op and timed (`sharded`), and the
+100M-node configuration (`c5`; replicated on one GPU, row-sharded on 2+).
 
 ``--impl reference`` runs the reference's own CUDA op (built from its
-sources into oracle/_ref) on the same workload through its public API; rank
-0 only.  The CPU baseline (rank 0, N=1) is the sequential C oracle on a
+sources into oracle/_ref) on the same workload through its public API, on
+every rank (each rank times its own 1024 roots).  The CPU baseline (rank 0, N=1) is the sequential C oracle on a
 bounded sample of the same workload.
 """
 
@@ -779,6 +783,38 @@ def persistent_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     }
 
 
+def allreduce_leg(w, inp: Inputs, args, dist: Dist, base_ms_per_step: float) -> dict:
+    """The replicated mode's data-parallel training step (2+ GPUs): the
+    same timed step followed by an NCCL all-reduce (sum) of the dense N x D
+    feature gradient over the ranks, so that every rank holds the gradient of
+    the whole global batch.  Device-timed, max over ranks."""
+    import fusesampleagg_b200 as fsa
+
+    launches0 = fsa.launch_count()
+    step = with_gradient_allreduce(make_step(fsa, w, inp, batch_offset=True), inp)
+    ms, _ = timed(step, args.steps, args.warmup, dist)
+    launches = (fsa.launch_count() - launches0) * args.steps // (args.steps + args.warmup)
+    units = w.batch * dist.world * args.steps
+    grad_bytes = 4 * inp.x.numel()
+    per_step = ms / args.steps
+    ar_ms = max(per_step - base_ms_per_step, 0.0)
+    return {
+        "value": units / (ms / 1000.0),
+        "unit": "roots/s",
+        "ms_per_step": per_step,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "gpu_launches": launches,
+        "allreduce_bytes": grad_bytes,
+        "allreduce_ms_per_step": ar_ms,
+        "allreduce_bus_gbs": (2.0 * (dist.world - 1) / dist.world * grad_bytes / (ar_ms * 1e-3)
+                              / 1e9) if ar_ms > 0 else None,
+        "mode": ("replicated features, roots partitioned with batch_offset, then an NCCL "
+                 "all-reduce of the dense feature gradient on the compute stream every step "
+                 "(the reference's data-parallel usage with torch.distributed)"),
+    }
+
+
 def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     """The row-sharded mode on the same global batch (2+ GPUs): this rank's
     ids and outputs against the replicated op's for the same slice, bit for
@@ -1136,6 +1172,8 @@ def run(args) -> None:
         # after every step has run).
         result["repo_libraries_mapped"] = check_reference_arm_libraries()
     if args.impl == "ours" and feats is None and not args.allreduce_grad:
+        if world >= 2 and not args.no_allreduce_leg:
+            result["replicated_allreduce"] = allreduce_leg(w, inp, args, dist, ms / args.steps)
         if world >= 2 and not args.no_sharded_leg:
             result["sharded"] = sharded_leg(w, inp, args, dist)
         if not args.no_c5 and args.workload != "c5_2hop_100m":
@@ -1269,6 +1307,9 @@ def main() -> None:
     p.add_argument("--cpu-budget", type=float, default=12.0)
     p.add_argument("--sharded", action="store_true",
                    help="row-shard the features over the ranks (peer reads over NVLink)")
+    p.add_argument("--no-allreduce-leg", action="store_true",
+                   help="on 2+ GPUs, skip the replicated step with the NCCL all-reduce of the "
+                        "dense feature gradient")
     p.add_argument("--no-sharded-leg", action="store_true",
                    help="on 2+ GPUs, skip the row-sharded check and timing after the main "
                         "measurement")
