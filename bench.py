@@ -670,7 +670,9 @@ def sharded_api(inp: Inputs, w):
     start, stop = sharding.shard_span(inp.n, int(os.environ.get("RANK", "0")),
                                       int(os.environ.get("WORLD_SIZE", "1")))
     local = inp.x.detach()[start:stop].clone().requires_grad_(True)
-    feats = sharding.ShardedFeatures(local, inp.n)
+    k1, k2 = w.fanouts
+    feats = sharding.ShardedFeatures(local, inp.n,
+                                     exchange_bytes=sharding.exchange_bytes(w.batch, k1, k2, w.dim))
     # the whole table is not needed any more: keep a 1-row stand-in so that
     # the steps' `x.grad = None` still works
     inp.x = torch.zeros((1, w.dim), device=local.device, requires_grad=True)
@@ -829,7 +831,8 @@ def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     k1, k2 = w.fanouts
     start, stop = sharding.shard_span(inp.n, dist.rank, dist.world)
     feats = sharding.ShardedFeatures(inp.x.detach()[start:stop].clone().requires_grad_(True),
-                                     inp.n)
+                                     inp.n,
+                                     exchange_bytes=sharding.exchange_bytes(w.batch, k1, k2, w.dim))
     exact = True
     checked = min(4, len(inp.frontiers))
     with torch.no_grad():
@@ -872,6 +875,11 @@ def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     launches0 = fsa.launch_count()
     ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
     launches = (fsa.launch_count() - launches0) * args.steps // (args.steps + args.warmup)
+    # the same steps with the backward sent as one remote red.add per
+    # contribution (every rank switches together)
+    feats.pull = False
+    push_ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
+    feats.pull = True
     feats.close()
     del feats
     torch.cuda.empty_cache()
@@ -890,10 +898,13 @@ def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
                        "replicated gradient, rtol 1e-5 / atol 1e-6"),
         "grad_max_abs_err_rank0": max_err,
         "gpu_launches": launches,
+        "push": {"value": units / (push_ms / 1000.0), "ms_per_step": push_ms / args.steps,
+                 "backward": "one red.add per remote contribution over NVLink"},
         "mode": ("feature rows and their gradient block-sharded over the GPUs: remote rows "
-                 "read and gradient added over NVLink through peer pointers (plain loads and "
-                 "red.add, no multicast); one-float NCCL all-reduce after forward and "
-                 "backward as the cross-GPU ordering"),
+                 "read over NVLink through peer pointers (plain loads, no multicast); backward "
+                 "computed by the owners: every rank publishes its saved ids and upstream "
+                 "gradient in an exchange region, every rank adds its rows' contributions "
+                 "from all regions; one-float NCCL all-reduces order the GPUs"),
     }
 
 
@@ -922,7 +933,15 @@ def c5_leg(args, dist: Dist, dev) -> dict:
         sampler.start()
     ms, _ = timed(make_step(step_api, w5, inp, batch_offset=True), steps, warmup, dist, sampler)
     clocks = sampler.stop() if sampler else None
+    push = None
     if feats is not None:
+        # the backward as one remote red.add per contribution, for comparison
+        feats.pull = False
+        push_ms, _ = timed(make_step(step_api, w5, inp, batch_offset=True), steps, warmup, dist)
+        feats.pull = True
+        push = {"value": w5.batch * dist.world * steps / (push_ms / 1000.0),
+                "ms_per_step": push_ms / steps,
+                "backward": "one red.add per remote contribution over NVLink"}
         feats.close()
     units = w5.batch * dist.world * steps
     out = {
@@ -936,8 +955,9 @@ def c5_leg(args, dist: Dist, dev) -> dict:
                    "roots_per_gpu": w5.batch, "global_batch": w5.batch * dist.world,
                    "graph_identical_across_ranks": same_graph},
         "mode": ("replicated features on one GPU" if feats is None else
-                 f"row-sharded features over {dist.world} GPUs (gradient owner-sharded over "
-                 "NVLink)"),
+                 f"row-sharded features over {dist.world} GPUs (gradient computed by the "
+                 "owners from every rank's published ids and upstream gradient)"),
+        "push": push,
         "setup_s": round(setup_s, 1),
         "clocks": clocks,
     }

@@ -59,6 +59,12 @@ SIGNATURES = {
                                                             [_i64, _i64, _i32, _i32]),
     "fsa_sample_agg_2hop_backward_sorted": (
         _int, [_p, _p, _p, _i64, _i64, _i32, _i32, _p, _i64, _p, ctypes.c_size_t, _p]),
+    "fsa_exchange_bytes": (ctypes.c_size_t, [_i64, _i32, _i32, _i64]),
+    "fsa_sharded_publish_2hop": (_int, [_p, ctypes.c_size_t, _p, _p, _p, _i64, _i64, _i32, _i32,
+                                        _p]),
+    "fsa_sample_agg_2hop_backward_sharded_pull": (
+        _int, [ctypes.POINTER(_p), ctypes.c_size_t, _i32, _i32, _p, _i64, _i64, _i64, _i32, _i32,
+               _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),
     "fsa_zero_rows_f32": (_int, [_p, _i64, _i64, _p, _i64, _p]),
     "fsa_phase_timing": (_int, [_int]),

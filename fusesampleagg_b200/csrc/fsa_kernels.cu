@@ -2381,3 +2381,266 @@ int fsa_sample_agg_2hop_forward_noalloc(const int32_t* rowptr, const int32_t* co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Row-sharded 2-hop backward where the owner computes (no counterpart in the
+// reference)
+// ---------------------------------------------------------------------------
+//
+// Every rank publishes its step's saved ids and upstream gradient into its
+// exchange region (mapped into every peer over CUDA IPC); after a
+// cross-device barrier each rank reads every region and adds the
+// contributions to its own rows into its own gradient shard.  Per root a
+// rank reads 4 (f1 + f1 f2) + 4 D bytes from each peer instead of sending
+// 4 D bytes of red.add per remote contribution.
+
+namespace {
+
+constexpr int64_t kExchangeHeader = 256;
+constexpr int kThreadsPublish = 256;
+constexpr int kThreadsPull = 128;
+constexpr int kPullCtasPerSm = 16;
+
+// Bytes of one root's record: samples1 and samples2 (int32), padded to 16
+// bytes, then the upstream gradient row (float), padded to 16 bytes.
+__host__ __device__ inline int64_t exchange_ids_bytes(int k1, int k2) {
+  return (4 * (static_cast<int64_t>(k1) + static_cast<int64_t>(k1) * k2) + 15) & ~int64_t{15};
+}
+
+__host__ __device__ inline int64_t exchange_root_bytes(int k1, int k2, int64_t D) {
+  return exchange_ids_bytes(k1, k2) + ((4 * D + 15) & ~int64_t{15});
+}
+
+struct PublishArgs {
+  unsigned char* region;
+  const float* grad_out;
+  const int32_t* samples1;
+  const int32_t* samples2;
+  int64_t batch_size;  // roots published (0 when the call has no contributions)
+  int64_t feature_dim;
+  int fanout1;
+  int fanout2;
+  int64_t stride;
+  int64_t ids_bytes;
+};
+
+// CTA per root (grid-stride): the root's record; block 0 writes the header
+// (the number of roots).
+template <int V>
+__global__ void __launch_bounds__(kThreadsPublish) fsa_exchange_publish_kernel(const PublishArgs a) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *reinterpret_cast<long long*>(a.region) = static_cast<long long>(a.batch_size);
+  }
+  const int k1 = a.fanout1;
+  const int k12 = k1 * a.fanout2;
+  const int64_t dvec = a.feature_dim / V;
+  for (int64_t b = blockIdx.x; b < a.batch_size; b += gridDim.x) {
+    unsigned char* rec = a.region + kExchangeHeader + b * a.stride;
+    int32_t* ids = reinterpret_cast<int32_t*>(rec);
+    for (int e = threadIdx.x; e < k1; e += blockDim.x) ids[e] = a.samples1[b * k1 + e];
+    for (int e = threadIdx.x; e < k12; e += blockDim.x) ids[k1 + e] = a.samples2[b * k12 + e];
+    float* g = reinterpret_cast<float*>(rec + a.ids_bytes);
+    for (int64_t v = threadIdx.x; v < dvec; v += blockDim.x) {
+      store_vec(g + v * V, load_vec<V>(a.grad_out + b * a.feature_dim + v * V));
+    }
+  }
+}
+
+struct PullArgs {
+  const unsigned char* regions[FSA_MAX_SHARDS];
+  int64_t cap_roots;  // records that fit one region
+  int num_shards;
+  int shard;          // this device's shard
+  float* grad;        // this device's gradient shard
+  int64_t shard_rows;
+  int64_t num_nodes;
+  int64_t feature_dim;
+  int fanout1;
+  int fanout2;
+  int64_t stride;
+  int64_t ids_bytes;
+};
+
+// Units are (region, root) pairs, regions interleaved so that concurrent
+// CTAs read from every peer.  A CTA copies the root's ids into shared
+// memory, counts each slot's valid ids and the ids this shard owns, counts
+// the non-empty slots (fused_sample_agg.cu:229-240) with ballots, then adds
+// (grad_out / nonempty) / valid of every owned id's slot into its row with
+// red.global.add (fused_sample_agg.cu:241-271).
+template <int V>
+__global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
+    fsa_2hop_backward_pull_kernel(const PullArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ long long s_roots[FSA_MAX_SHARDS];
+  const int k1 = a.fanout1;
+  const int k2 = a.fanout2;
+  const int k12 = k1 * k2;
+  int* ids = reinterpret_cast<int*>(smem_raw);  // [k1 + k12]: samples1, then samples2
+  int* valid = ids + k1 + k12;                   // [k1]
+  int* mine = valid + k1;                        // [k1]
+  const int tid = threadIdx.x;
+  const int nthreads = blockDim.x;
+  const int lane = tid & 31;
+  for (int s = tid; s < a.num_shards; s += nthreads) {
+    const long long n = *reinterpret_cast<const long long*>(a.regions[s]);
+    s_roots[s] = n < 0 ? 0 : (n > a.cap_roots ? a.cap_roots : n);
+  }
+  __syncthreads();
+  const int64_t D = a.feature_dim;
+  const int64_t dvec = D / V;
+  const int64_t N = a.num_nodes;
+  const uint32_t rows = static_cast<uint32_t>(a.shard_rows);
+  const uint32_t me = static_cast<uint32_t>(a.shard);
+  const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;
+  const int64_t units = a.cap_roots * a.num_shards;
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const int s = static_cast<int>(u % a.num_shards);
+    const int64_t b = u / a.num_shards;
+    if (b >= s_roots[s]) continue;  // the same for the whole CTA
+    const unsigned char* rec = a.regions[s] + kExchangeHeader + b * a.stride;
+    const int32_t* rids = reinterpret_cast<const int32_t*>(rec);
+    for (int e = tid; e < k1 + k12; e += nthreads) ids[e] = rids[e];
+    __syncthreads();
+    for (int i = tid; i < k1; i += nthreads) {
+      int cnt = 0;
+      int own = 0;
+      for (int j = 0; j < k2; ++j) {
+        const int32_t leaf = ids[k1 + i * k2 + j];
+        if (leaf < 0) continue;
+        ++cnt;
+        if (leaf >= N) {
+          flag_status(FSA_STATUS_BAD_NEIGHBOR);
+        } else if (static_cast<uint32_t>(leaf) / rows == me) {
+          ++own;
+        }
+      }
+      valid[i] = cnt;
+      mine[i] = own;
+    }
+    __syncthreads();
+    int nonempty = 0;
+    for (int i0 = 0; i0 < k1; i0 += 32) {
+      const int i = i0 + lane;
+      nonempty += __popc(__ballot_sync(0xffffffffU, i < k1 && ids[i] >= 0 && valid[i] > 0));
+    }
+    if (nonempty > 0) {
+      const float ne = static_cast<float>(nonempty);
+      const float* go = reinterpret_cast<const float*>(rec + a.ids_bytes);
+      const int64_t items = static_cast<int64_t>(k1) * dvec;
+      for (int64_t it = tid; it < items; it += nthreads) {
+        const int i = static_cast<int>(it / dvec);
+        if (mine[i] == 0) continue;
+        const int64_t v = it - static_cast<int64_t>(i) * dvec;
+        VecF<V> g = load_vec<V>(go + v * V);
+        const float vc = static_cast<float>(valid[i]);
+#pragma unroll
+        for (int c = 0; c < V; ++c) g.v[c] = (g.v[c] / ne) / vc;
+        const int* leaves = ids + k1 + i * k2;
+        for (int j = 0; j < k2; ++j) {
+          const int32_t leaf = leaves[j];
+          if (leaf < 0 || leaf >= N || static_cast<uint32_t>(leaf) / rows != me) continue;
+          red_add<V>(a.grad + (static_cast<int64_t>(leaf) - lo) * D + v * V, g);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+bool exchange_args_ok(int64_t batch_size, int32_t fanout1, int32_t fanout2, int64_t feature_dim) {
+  return batch_size >= 0 && fanout1 >= 0 && fanout2 >= 0 && feature_dim >= 0 &&
+         static_cast<int64_t>(fanout1) + static_cast<int64_t>(fanout1) * fanout2 <=
+             FSA_MAX_2HOP_ENTRIES &&
+         feature_dim <= (int64_t{1} << 40) && batch_size <= (int64_t{1} << 40);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fsa_exchange_bytes(int64_t batch_size, int32_t fanout1, int32_t fanout2,
+                          int64_t feature_dim) {
+  if (!exchange_args_ok(batch_size, fanout1, fanout2, feature_dim)) return 0;
+  return static_cast<size_t>(kExchangeHeader +
+                             batch_size * exchange_root_bytes(fanout1, fanout2, feature_dim));
+}
+
+int fsa_sharded_publish_2hop(void* exchange, size_t exchange_bytes, const float* grad_out,
+                             const int32_t* samples1, const int32_t* samples2,
+                             int64_t batch_size, int64_t feature_dim, int32_t fanout1,
+                             int32_t fanout2, void* stream) {
+  if (!exchange_args_ok(batch_size, fanout1, fanout2, feature_dim)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  if (exchange == nullptr || !aligned(exchange, 256) ||
+      exchange_bytes < fsa_exchange_bytes(batch_size, fanout1, fanout2, feature_dim)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  const bool work = batch_size > 0 && fanout1 > 0 && fanout2 > 0 && feature_dim > 0;
+  if (work && (grad_out == nullptr || samples1 == nullptr || samples2 == nullptr)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  const int64_t stride = exchange_root_bytes(fanout1, fanout2, feature_dim);
+  const PublishArgs pa{static_cast<unsigned char*>(exchange), grad_out, samples1, samples2,
+                       work ? batch_size : 0, feature_dim, fanout1, fanout2, stride,
+                       exchange_ids_bytes(fanout1, fanout2)};
+  const int grid = grid_for(work ? batch_size : 1);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (feature_dim % 4 == 0 && aligned(grad_out, 16)) {
+    return launch(fsa_exchange_publish_kernel<4>, grid, kThreadsPublish, 0, s, pa);
+  }
+  return launch(fsa_exchange_publish_kernel<1>, grid, kThreadsPublish, 0, s, pa);
+}
+
+int fsa_sample_agg_2hop_backward_sharded_pull(const void* const* exchanges,
+                                              size_t exchange_bytes, int32_t num_shards,
+                                              int32_t shard, float* grad_shard,
+                                              int64_t shard_rows, int64_t num_nodes,
+                                              int64_t feature_dim, int32_t fanout1,
+                                              int32_t fanout2, void* stream) {
+  if (!exchange_args_ok(0, fanout1, fanout2, feature_dim) || exchanges == nullptr ||
+      num_shards < 1 || num_shards > FSA_MAX_SHARDS || shard < 0 || shard >= num_shards ||
+      shard_rows < 1 || shard_rows > 0x7fffffffLL || num_nodes < 0 ||
+      num_nodes > shard_rows * num_shards || exchange_bytes < static_cast<size_t>(kExchangeHeader)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  PullArgs pa{};
+  for (int k = 0; k < num_shards; ++k) {
+    if (exchanges[k] == nullptr || !aligned(exchanges[k], 256)) return FSA_ERR_INVALID_ARGUMENT;
+    pa.regions[k] = static_cast<const unsigned char*>(exchanges[k]);
+  }
+  if (fanout1 == 0 || fanout2 == 0 || feature_dim == 0) return FSA_OK;
+  if (grad_shard == nullptr || !aligned(grad_shard, 4)) return FSA_ERR_INVALID_ARGUMENT;
+  const int64_t stride = exchange_root_bytes(fanout1, fanout2, feature_dim);
+  pa.cap_roots = (static_cast<int64_t>(exchange_bytes) - kExchangeHeader) / stride;
+  if (pa.cap_roots == 0) return FSA_OK;
+  pa.num_shards = num_shards;
+  pa.shard = shard;
+  pa.grad = grad_shard;
+  pa.shard_rows = shard_rows;
+  pa.num_nodes = num_nodes;
+  pa.feature_dim = feature_dim;
+  pa.fanout1 = fanout1;
+  pa.fanout2 = fanout2;
+  pa.stride = stride;
+  pa.ids_bytes = exchange_ids_bytes(fanout1, fanout2);
+  int sms = 0;
+  const int st = sm_count(&sms);
+  if (st != FSA_OK) return st;
+  const int64_t units = pa.cap_roots * num_shards;
+  const int64_t resident = static_cast<int64_t>(sms) * kPullCtasPerSm;
+  const int grid = grid_for(units < resident ? units : resident);
+  const int smem = 4 * (3 * fanout1 + fanout1 * fanout2);
+  auto s = static_cast<cudaStream_t>(stream);
+  // The records' gradient rows are 16-byte aligned; the shard's rows are
+  // when feature_dim % 4 == 0 and its base is.
+  if (feature_dim % 4 == 0 && aligned(grad_shard, 16)) {
+    return launch(fsa_2hop_backward_pull_kernel<4>, grid, kThreadsPull, smem, s, pa);
+  }
+  if (feature_dim % 2 == 0 && aligned(grad_shard, 8)) {
+    return launch(fsa_2hop_backward_pull_kernel<2>, grid, kThreadsPull, smem, s, pa);
+  }
+  return launch(fsa_2hop_backward_pull_kernel<1>, grid, kThreadsPull, smem, s, pa);
+}
+
+}  // extern "C"

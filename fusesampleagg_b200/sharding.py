@@ -69,9 +69,18 @@ class ShardedFeatures:
     the kernels read remote feature rows and add into remote gradient rows
     directly over NVLink.  Call `close()` on every rank (collective) before
     the process group is destroyed.
+
+    With ``exchange_bytes > 0`` (the same on every rank; see
+    `exchange_bytes`) every rank also shares an exchange region of that
+    size, and the backward is computed by the owners: each rank publishes
+    its saved ids and upstream gradient there, and after a device barrier
+    every rank adds the contributions to its own rows from all ranks'
+    regions (fsa_sample_agg_2hop_backward_sharded_pull) instead of sending
+    one red.add per remote contribution.  Every backward's batch must then
+    fit the region on every rank.
     """
 
-    def __init__(self, local: torch.Tensor, num_nodes: int, group=None):
+    def __init__(self, local: torch.Tensor, num_nodes: int, group=None, exchange_bytes: int = 0):
         import ctypes
 
         import torch.distributed as dist
@@ -94,6 +103,15 @@ class ShardedFeatures:
         self.dim = int(local.size(1))
         self.local = local.contiguous()
         self.grad = torch.zeros_like(self.local)
+        self.exchange_bytes = int(exchange_bytes)
+        if self.exchange_bytes < 0:
+            raise ValueError("exchange_bytes must be non-negative")
+        self.exchange = (torch.empty((self.exchange_bytes,), dtype=torch.uint8,
+                                     device=self.local.device)
+                         if self.exchange_bytes > 0 else None)
+        # owner-computed backward when there is an exchange region (the same
+        # setting on every rank: set it to False on all ranks for the push)
+        self.pull = self.exchange is not None
         self._flag = torch.zeros(1, device=self.local.device)
         self._device = self.local.device.index
         L = _lib.LIB
@@ -107,17 +125,20 @@ class ShardedFeatures:
             return h.raw, off.value
 
         shared = [None] * self.world
-        dist.all_gather_object(shared, (export(self.local), export(self.grad)), group=group)
+        mine = (export(self.local), export(self.grad),
+                export(self.exchange) if self.exchange is not None else None)
+        dist.all_gather_object(shared, mine, group=group)
         # Map every peer allocation once, into this device's address space.
         self._mapped = {}
-        xs, gs = [], []
-        for r, (xe, ge) in enumerate(shared):
+        xs, gs, es = [], [], []
+        for r, (xe, ge, ee) in enumerate(shared):
             if r == self.rank:
                 xs.append(self.local.data_ptr())
                 gs.append(self.grad.data_ptr())
+                es.append(self.exchange.data_ptr() if self.exchange is not None else 0)
                 continue
-            for e, out in ((xe, xs), (ge, gs)):
-                if e is None:  # an empty trailing shard: any aligned base
+            for e, out in ((xe, xs), (ge, gs), (ee, es)):
+                if e is None:  # an empty trailing shard (or no exchange): any aligned base
                     out.append(self.local.data_ptr())
                     continue
                 handle, off = e
@@ -130,6 +151,7 @@ class ShardedFeatures:
         ptrs = ctypes.c_void_p * self.world
         self.x_ptrs = ptrs(*xs)
         self.grad_ptrs = ptrs(*gs)
+        self.exchange_ptrs = ptrs(*es) if self.exchange is not None else None
 
     def device_barrier(self) -> None:
         """Orders the GPUs: the current stream of every rank waits until every
@@ -151,8 +173,45 @@ class ShardedFeatures:
         for base in self._mapped.values():
             _lib.check(_lib.LIB.fsa_ipc_close(base, self._device), "fsa_ipc_close")
         self._mapped.clear()
-        self.x_ptrs = self.grad_ptrs = None
+        self.x_ptrs = self.grad_ptrs = self.exchange_ptrs = None
         dist.barrier(group=self.group)
+
+
+def exchange_bytes(batch_size: int, fanout1: int, fanout2: int, dim: int) -> int:
+    """Exchange-region bytes (`ShardedFeatures(exchange_bytes=...)`) that a
+    rank's 2-hop backward of `batch_size` roots needs."""
+    from . import _lib
+
+    n = int(_lib.LIB.fsa_exchange_bytes(int(batch_size), int(fanout1), int(fanout2), int(dim)))
+    if n == 0:
+        raise ValueError("invalid batch size, fanouts or feature dimension")
+    return n
+
+
+def _backward_pull(feats: ShardedFeatures, g, s1, s2):
+    """Owner-computes backward: publish this rank's ids and upstream
+    gradient, wait for every rank's, add the contributions to this rank's
+    rows from all regions."""
+    from . import _lib, _stream_handle
+
+    L = _lib.LIB
+    B, D = g.shape
+    k1, k2 = s1.size(1), s2.size(2)
+    need = int(L.fsa_exchange_bytes(B, k1, k2, D))
+    if need == 0 or need > feats.exchange_bytes:
+        raise RuntimeError(f"a backward of {B} roots at fanouts ({k1}, {k2}) needs an exchange "
+                           f"region of {need} bytes; this ShardedFeatures has "
+                           f"{feats.exchange_bytes}")
+    stream = _stream_handle(g.device)
+    _lib.check(L.fsa_sharded_publish_2hop(feats.exchange.data_ptr(), feats.exchange_bytes,
+                                          g.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1,
+                                          k2, stream), "fsa_sharded_publish_2hop")
+    # every rank's region holds this step's records
+    feats.device_barrier()
+    _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
+        feats.exchange_ptrs, feats.exchange_bytes, feats.world, feats.rank, feats.grad.data_ptr(),
+        feats.shard_rows, feats.num_nodes, D, k1, k2, stream),
+        "fsa_sample_agg_2hop_backward_sharded_pull")
 
 
 def _forward_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier, fanout1, fanout2,
@@ -223,12 +282,16 @@ class _Sharded2HopFn(torch.autograd.Function):
             g = grad_out.contiguous()
             B, D = g.shape
             with _DeviceGuard(g.device):
-                st = _lib.LIB.fsa_sample_agg_2hop_backward_sharded(
-                    g.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, s1.size(1), s2.size(2),
-                    feats.grad_ptrs, feats.shard_rows, feats.world, feats.num_nodes,
-                    _stream_handle(g.device))
-                _lib.check(st, "fsa_sample_agg_2hop_backward_sharded")
-            # every rank's additions into this rank's shard are complete
+                if feats.pull and feats.exchange is not None:
+                    _backward_pull(feats, g, s1, s2)
+                else:
+                    st = _lib.LIB.fsa_sample_agg_2hop_backward_sharded(
+                        g.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, s1.size(1),
+                        s2.size(2), feats.grad_ptrs, feats.shard_rows, feats.world,
+                        feats.num_nodes, _stream_handle(g.device))
+                    _lib.check(st, "fsa_sample_agg_2hop_backward_sharded")
+            # every rank's additions into this rank's shard are complete (and,
+            # owner-computed, every rank has read the exchange regions)
             feats.device_barrier()
         ctx.feats = None
         return (None,) * 9
@@ -241,8 +304,9 @@ def fused_sample_agg_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier,
     Same ids and outputs as ``fused_sample_agg_2hop`` on the whole table
     (with the same `batch_offset`).  When ``feats.local.requires_grad`` the
     forward zeroes ``feats.grad`` and the backward adds this rank's roots'
-    feature gradients into the owning ranks' ``feats.grad`` (over NVLink);
-    after the backward, ``feats.grad`` on every rank holds the gradient of its
+    feature gradients into the owning ranks' ``feats.grad`` (over NVLink;
+    with an exchange region every owner computes its rows' share from all
+    ranks' published ids and upstream gradients instead); after the backward, ``feats.grad`` on every rank holds the gradient of its
     rows summed over all ranks' roots.  Collective when training: every rank
     must call forward and backward the same number of times.
     """

@@ -243,6 +243,43 @@ FSA_API int fsa_sample_agg_2hop_backward_sharded(const float* grad_out, const in
                                                  int64_t num_nodes, void* stream);
 
 /*
+ * Row-sharded 2-hop backward where each device computes its own rows'
+ * gradient ("owner computes"; no counterpart in the reference).  The
+ * alternative to fsa_sample_agg_2hop_backward_sharded, which sends one
+ * red.add per remote contribution over NVLink: here every device first
+ * publishes its saved ids and upstream gradient into its EXCHANGE REGION
+ * (fsa_sharded_publish_2hop), the caller orders the devices (every region
+ * written before any device reads one), and then every device reads all
+ * regions -- its own and its peers', mapped over CUDA IPC -- and adds the
+ * contributions to the rows it owns into its own gradient shard
+ * (fsa_sample_agg_2hop_backward_sharded_pull).  Per root a device reads
+ * 4 (fanout1 + fanout1 fanout2) + 4 feature_dim bytes from each peer.
+ *
+ * Region layout (exchange_bytes each, the same size on every device, base
+ * aligned to 256 bytes): an int64 root count at offset 0, then from byte
+ * 256 one record per root of fsa_exchange_bytes(1, ...) - 256 bytes:
+ * samples1[fanout1] and samples2[fanout1][fanout2] (int32), padded to 16
+ * bytes, then grad_out[feature_dim] (float), padded to 16 bytes.
+ * fsa_exchange_bytes(batch_size, ...) is the region size a batch needs (0
+ * for invalid arguments).  The pull call adds into grad_shard (rows
+ * [shard * shard_rows, ...), pre-zeroed or accumulating), the same result
+ * as the push entry point up to the order of the additions.  The caller
+ * orders the devices again before any region is rewritten.
+ */
+FSA_API size_t fsa_exchange_bytes(int64_t batch_size, int32_t fanout1, int32_t fanout2,
+                                  int64_t feature_dim);
+FSA_API int fsa_sharded_publish_2hop(void* exchange, size_t exchange_bytes, const float* grad_out,
+                                     const int32_t* samples1, const int32_t* samples2,
+                                     int64_t batch_size, int64_t feature_dim, int32_t fanout1,
+                                     int32_t fanout2, void* stream);
+FSA_API int fsa_sample_agg_2hop_backward_sharded_pull(const void* const* exchanges,
+                                                      size_t exchange_bytes, int32_t num_shards,
+                                                      int32_t shard, float* grad_shard,
+                                                      int64_t shard_rows, int64_t num_nodes,
+                                                      int64_t feature_dim, int32_t fanout1,
+                                                      int32_t fanout2, void* stream);
+
+/*
  * Sharing shards between processes (one process per GPU), no counterpart in
  * the reference.  fsa_ipc_export writes the CUDA IPC handle
  * (FSA_IPC_HANDLE_BYTES bytes) of the allocation holding `ptr` and ptr's

@@ -201,3 +201,34 @@ def test_torch_binding_rejects_cpu_tensors_before_cuda():
         _fsa_torch.sample_agg_2hop_with_samples(rp, rp, x, rp, 2, 2, 1, 0)
     with pytest.raises(RuntimeError, match="CUDA"):
         _fsa_torch.sample_agg_with_samples(rp, rp, x, rp, 2, 1, 0)
+
+
+def test_exchange_bytes_layout():
+    """Owner-computes sharded backward's region size: a 256-byte header,
+    then per root 4 (f1 + f1 f2) bytes of ids and 4 D bytes of upstream
+    gradient, each padded to 16 bytes."""
+    assert L.fsa_exchange_bytes(0, 15, 10, 100) == 256
+    assert L.fsa_exchange_bytes(1024, 15, 10, 100) == 256 + 1024 * (672 + 400)
+    assert L.fsa_exchange_bytes(3, 2, 1, 3) == 256 + 3 * (16 + 16)
+    assert L.fsa_exchange_bytes(-1, 15, 10, 100) == 0
+    assert L.fsa_exchange_bytes(4, 5, 2400, 8) == 0  # over the 12000-entry limit
+
+
+def test_exchange_entry_points_reject_bad_arguments_before_cuda():
+    fake = 1 << 20  # aligned, never dereferenced: every call returns first
+    assert L.fsa_sharded_publish_2hop(fake, 1024, fake, fake, fake, 64, 100, 15, 10,
+                                      NULL) == _lib.FSA_ERR_INVALID_ARGUMENT  # region too small
+    assert L.fsa_sharded_publish_2hop(fake + 8, 1 << 20, fake, fake, fake, 4, 100, 15, 10,
+                                      NULL) == _lib.FSA_ERR_INVALID_ARGUMENT  # misaligned
+    assert L.fsa_sharded_publish_2hop(fake, 1 << 20, NULL, fake, fake, 4, 100, 15, 10,
+                                      NULL) == _lib.FSA_ERR_INVALID_ARGUMENT  # no gradient
+    ptrs = (ctypes.c_void_p * 2)(fake, fake)
+    pull = L.fsa_sample_agg_2hop_backward_sharded_pull
+    assert pull(ptrs, 1 << 20, 2, 2, fake, 10, 20, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert pull(ptrs, 1 << 20, 2, 0, fake, 10, 21, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert pull(ptrs, 100, 2, 0, fake, 10, 20, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    bad = (ctypes.c_void_p * 2)(fake, None)
+    assert pull(bad, 1 << 20, 2, 0, fake, 10, 20, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    # nothing to add: returns before any CUDA call
+    assert pull(ptrs, 1 << 20, 2, 0, fake, 10, 20, 8, 0, 2, NULL) == _lib.FSA_OK
+
