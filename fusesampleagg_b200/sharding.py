@@ -264,9 +264,11 @@ class _Sharded2HopFn(torch.autograd.Function):
                                             replay_seed, capture, batch_offset,
                                             feats.grad if capture else None)
         if capture:
-            # every rank's gradient shard is zero before any rank's backward
-            # adds into it
-            feats.device_barrier()
+            if not (feats.pull and feats.exchange is not None):
+                # every rank's gradient shard is zero before any rank's
+                # backward adds into it (owner-computed, only the owner adds
+                # into its shard, in stream order)
+                feats.device_barrier()
             ctx.save_for_backward(s1, s2)
         ctx.feats = feats
         ctx.capture = capture
@@ -291,7 +293,8 @@ class _Sharded2HopFn(torch.autograd.Function):
                         feats.num_nodes, _stream_handle(g.device))
                     _lib.check(st, "fsa_sample_agg_2hop_backward_sharded")
             # every rank's additions into this rank's shard are complete (and,
-            # owner-computed, every rank has read the exchange regions)
+            # owner-computed, every rank has read the exchange regions before
+            # any rank's next backward rewrites its own)
             feats.device_barrier()
         ctx.feats = None
         return (None,) * 9
