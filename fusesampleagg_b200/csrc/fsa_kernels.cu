@@ -2459,10 +2459,16 @@ struct PullArgs {
   int fanout2;
   int64_t stride;
   int64_t ids_bytes;
+  int64_t staged_bytes;  // bytes of each record copied to shared memory (ids, or the whole record)
 };
 
+// Records up to this size are copied to shared memory whole (ids and
+// upstream gradient row in one round of 16-byte loads); longer ones keep
+// the gradient row in the region.
+constexpr int64_t kPullStageBytes = 16 * 1024;
+
 // Units are (region, root) pairs, regions interleaved so that concurrent
-// CTAs read from every peer.  A CTA copies the root's ids into shared
+// CTAs read from every peer.  A CTA copies the root's record into shared
 // memory, counts each slot's valid ids and the ids this shard owns, counts
 // the non-empty slots (fused_sample_agg.cu:229-240) with ballots, then adds
 // (grad_out / nonempty) / valid of every owned id's slot into its row with
@@ -2474,10 +2480,11 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   __shared__ long long s_roots[FSA_MAX_SHARDS];
   const int k1 = a.fanout1;
   const int k2 = a.fanout2;
-  const int k12 = k1 * k2;
-  int* ids = reinterpret_cast<int*>(smem_raw);  // [k1 + k12]: samples1, then samples2
-  int* valid = ids + k1 + k12;                   // [k1]
-  int* mine = valid + k1;                        // [k1]
+  int* ids = reinterpret_cast<int*>(smem_raw);  // the record: samples1, samples2 (, gradient)
+  int* valid = reinterpret_cast<int*>(smem_raw + a.staged_bytes);  // [k1]
+  int* mine = valid + k1;                                          // [k1] owned ids per slot
+  int* owned = mine + k1;  // [k1][k2] local rows of the owned ids, slot by slot
+  const bool staged_grad = a.staged_bytes == a.stride;
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
   const int lane = tid & 31;
@@ -2498,8 +2505,11 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
     const int64_t b = u / a.num_shards;
     if (b >= s_roots[s]) continue;  // the same for the whole CTA
     const unsigned char* rec = a.regions[s] + kExchangeHeader + b * a.stride;
-    const int32_t* rids = reinterpret_cast<const int32_t*>(rec);
-    for (int e = tid; e < k1 + k12; e += nthreads) ids[e] = rids[e];
+    {
+      const int4* src = reinterpret_cast<const int4*>(rec);
+      int4* dst = reinterpret_cast<int4*>(smem_raw);
+      for (int64_t q = tid; q < a.staged_bytes / 16; q += nthreads) dst[q] = src[q];
+    }
     __syncthreads();
     for (int i = tid; i < k1; i += nthreads) {
       int cnt = 0;
@@ -2511,7 +2521,7 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
         if (leaf >= N) {
           flag_status(FSA_STATUS_BAD_NEIGHBOR);
         } else if (static_cast<uint32_t>(leaf) / rows == me) {
-          ++own;
+          owned[i * k2 + own++] = static_cast<int>(leaf - lo);
         }
       }
       valid[i] = cnt;
@@ -2525,7 +2535,8 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
     }
     if (nonempty > 0) {
       const float ne = static_cast<float>(nonempty);
-      const float* go = reinterpret_cast<const float*>(rec + a.ids_bytes);
+      const float* go = reinterpret_cast<const float*>(
+          (staged_grad ? static_cast<const unsigned char*>(smem_raw) : rec) + a.ids_bytes);
       const int64_t items = static_cast<int64_t>(k1) * dvec;
       for (int64_t it = tid; it < items; it += nthreads) {
         const int i = static_cast<int>(it / dvec);
@@ -2535,15 +2546,119 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
         const float vc = static_cast<float>(valid[i]);
 #pragma unroll
         for (int c = 0; c < V; ++c) g.v[c] = (g.v[c] / ne) / vc;
-        const int* leaves = ids + k1 + i * k2;
-        for (int j = 0; j < k2; ++j) {
-          const int32_t leaf = leaves[j];
-          if (leaf < 0 || leaf >= N || static_cast<uint32_t>(leaf) / rows != me) continue;
-          red_add<V>(a.grad + (static_cast<int64_t>(leaf) - lo) * D + v * V, g);
+        const int* rows_i = owned + i * k2;
+        for (int m = 0; m < mine[i]; ++m) {
+          red_add<V>(a.grad + static_cast<int64_t>(rows_i[m]) * D + v * V, g);
         }
       }
     }
     __syncthreads();
+  }
+}
+
+// Per-warp shared memory up to which a warp takes a unit alone
+// (fsa_2hop_backward_pull_warp_kernel): no CTA barriers between a unit's
+// record load, counts and additions, and every resident warp has a record
+// in flight.
+constexpr int64_t kPullWarpSliceBytes = 4096;
+
+// A warp's shared memory in fsa_2hop_backward_pull_warp_kernel: the staged
+// record, then valid / owned counts and the owned slots ([3][k1] int) and
+// the owned ids' local rows ([k1][k2] int), padded to 16 bytes.
+__host__ __device__ inline int64_t pull_warp_slice(int64_t staged, int k1, int k2) {
+  return staged + 16 * ((4 * (3 * static_cast<int64_t>(k1) + static_cast<int64_t>(k1) * k2) + 15) / 16);
+}
+
+// The same additions as fsa_2hop_backward_pull_kernel with one warp per
+// (region, root) unit: the warp copies the whole record into its own slice
+// of shared memory, lane i counts slot i, the warp counts the non-empty
+// slots with ballots and its lanes add the items of the owned ids.
+template <int V>
+__global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
+    fsa_2hop_backward_pull_warp_kernel(const PullArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ long long s_roots[FSA_MAX_SHARDS];
+  const int k1 = a.fanout1;
+  const int k2 = a.fanout2;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = static_cast<int>(blockDim.x >> 5);
+  for (int s = tid; s < a.num_shards; s += blockDim.x) {
+    const long long n = *reinterpret_cast<const long long*>(a.regions[s]);
+    s_roots[s] = n < 0 ? 0 : (n > a.cap_roots ? a.cap_roots : n);
+  }
+  __syncthreads();
+  const int64_t slice = pull_warp_slice(a.staged_bytes, k1, k2);
+  unsigned char* mem = smem_raw + warp * slice;
+  const int* ids = reinterpret_cast<const int*>(mem);  // samples1, samples2, gradient row
+  int* valid = reinterpret_cast<int*>(mem + a.staged_bytes);  // [k1]
+  int* mine = valid + k1;                                     // [k1] owned ids per slot
+  int* oslot = mine + k1;                                     // [k1] slots with owned ids
+  int* owned = oslot + k1;  // [k1][k2] local rows of the owned ids, slot by slot
+  const float* go = reinterpret_cast<const float*>(mem + a.ids_bytes);
+  const int dvec = static_cast<int>(a.feature_dim / V);
+  const int64_t D = a.feature_dim;
+  const int64_t N = a.num_nodes;
+  const uint32_t rows = static_cast<uint32_t>(a.shard_rows);
+  const uint32_t me = static_cast<uint32_t>(a.shard);
+  const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;
+  const int64_t units = a.cap_roots * a.num_shards;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * nwarps + warp; u < units;
+       u += static_cast<int64_t>(gridDim.x) * nwarps) {
+    const int s = static_cast<int>(u % a.num_shards);
+    const int64_t b = u / a.num_shards;
+    if (b >= s_roots[s]) continue;  // the same for the whole warp
+    {
+      const int4* src =
+          reinterpret_cast<const int4*>(a.regions[s] + kExchangeHeader + b * a.stride);
+      int4* dst = reinterpret_cast<int4*>(mem);
+      for (int q = lane; q < static_cast<int>(a.staged_bytes / 16); q += 32) dst[q] = src[q];
+    }
+    __syncwarp();
+    int nonempty = 0;
+    int nowned = 0;  // slots with owned ids, listed in oslot
+    for (int i0 = 0; i0 < k1; i0 += 32) {
+      const int i = i0 + lane;
+      int cnt = 0;
+      int own = 0;
+      if (i < k1) {
+        for (int j = 0; j < k2; ++j) {
+          const int32_t leaf = ids[k1 + i * k2 + j];
+          if (leaf < 0) continue;
+          ++cnt;
+          if (leaf >= N) {
+            flag_status(FSA_STATUS_BAD_NEIGHBOR);
+          } else if (static_cast<uint32_t>(leaf) / rows == me) {
+            owned[i * k2 + own++] = static_cast<int>(leaf - lo);
+          }
+        }
+        valid[i] = cnt;
+        mine[i] = own;
+      }
+      nonempty += __popc(__ballot_sync(0xffffffffU, i < k1 && ids[i] >= 0 && cnt > 0));
+      const unsigned has = __ballot_sync(0xffffffffU, own > 0);
+      if (own > 0) oslot[nowned + __popc(has & ((1U << lane) - 1U))] = i;
+      nowned += __popc(has);
+    }
+    __syncwarp();
+    if (nonempty > 0 && nowned > 0) {
+      const float ne = static_cast<float>(nonempty);
+      for (int it = lane; it < nowned * dvec; it += 32) {
+        const int t = it / dvec;
+        const int v = it - t * dvec;
+        const int i = oslot[t];
+        VecF<V> g = load_vec<V>(go + v * V);
+        const float vc = static_cast<float>(valid[i]);
+#pragma unroll
+        for (int c = 0; c < V; ++c) g.v[c] = (g.v[c] / ne) / vc;
+        const int* rows_i = owned + i * k2;
+        for (int m = 0; m < mine[i]; ++m) {
+          red_add<V>(a.grad + static_cast<int64_t>(rows_i[m]) * D + v * V, g);
+        }
+      }
+    }
+    __syncwarp();
   }
 }
 
@@ -2624,23 +2739,42 @@ int fsa_sample_agg_2hop_backward_sharded_pull(const void* const* exchanges,
   pa.fanout2 = fanout2;
   pa.stride = stride;
   pa.ids_bytes = exchange_ids_bytes(fanout1, fanout2);
+  pa.staged_bytes = stride <= kPullStageBytes ? stride : pa.ids_bytes;
   int sms = 0;
   const int st = sm_count(&sms);
   if (st != FSA_OK) return st;
   const int64_t units = pa.cap_roots * num_shards;
   const int64_t resident = static_cast<int64_t>(sms) * kPullCtasPerSm;
   const int grid = grid_for(units < resident ? units : resident);
-  const int smem = 4 * (3 * fanout1 + fanout1 * fanout2);
   auto s = static_cast<cudaStream_t>(stream);
   // The records' gradient rows are 16-byte aligned; the shard's rows are
   // when feature_dim % 4 == 0 and its base is.
-  if (feature_dim % 4 == 0 && aligned(grad_shard, 16)) {
-    return launch(fsa_2hop_backward_pull_kernel<4>, grid, kThreadsPull, smem, s, pa);
+  const int vec = feature_dim % 4 == 0 && aligned(grad_shard, 16)  ? 4
+                  : feature_dim % 2 == 0 && aligned(grad_shard, 8) ? 2
+                                                                    : 1;
+  const int64_t slice = pull_warp_slice(stride, fanout1, fanout2);
+  const int nwarps_sm = kPullCtasPerSm * (kThreadsPull / 32);
+  if (stride <= kPullStageBytes && slice <= kPullWarpSliceBytes &&
+      units >= static_cast<int64_t>(sms) * nwarps_sm) {
+    // a warp per unit, when the units fill every resident warp
+    pa.staged_bytes = stride;
+    const int nwarps = kThreadsPull / 32;
+    const int64_t wunits = (units + nwarps - 1) / nwarps;
+    const int wgrid = grid_for(wunits < resident ? wunits : resident);
+    const int wsmem = static_cast<int>(nwarps * slice);
+    switch (vec) {
+      case 4: return launch(fsa_2hop_backward_pull_warp_kernel<4>, wgrid, kThreadsPull, wsmem, s, pa);
+      case 2: return launch(fsa_2hop_backward_pull_warp_kernel<2>, wgrid, kThreadsPull, wsmem, s, pa);
+      default: return launch(fsa_2hop_backward_pull_warp_kernel<1>, wgrid, kThreadsPull, wsmem, s, pa);
+    }
   }
-  if (feature_dim % 2 == 0 && aligned(grad_shard, 8)) {
-    return launch(fsa_2hop_backward_pull_kernel<2>, grid, kThreadsPull, smem, s, pa);
+  const int smem =
+      static_cast<int>(pa.staged_bytes) + 4 * (2 * fanout1 + fanout1 * fanout2);
+  switch (vec) {
+    case 4: return launch(fsa_2hop_backward_pull_kernel<4>, grid, kThreadsPull, smem, s, pa);
+    case 2: return launch(fsa_2hop_backward_pull_kernel<2>, grid, kThreadsPull, smem, s, pa);
+    default: return launch(fsa_2hop_backward_pull_kernel<1>, grid, kThreadsPull, smem, s, pa);
   }
-  return launch(fsa_2hop_backward_pull_kernel<1>, grid, kThreadsPull, smem, s, pa);
 }
 
 }  // extern "C"

@@ -85,6 +85,8 @@ def run(name, dim, k1, k2, batches, world):
     ("powerlaw", 33, 8, 4, (128, 127, 128)),
     ("powerlaw", 6, 25, 10, (64, 64, 64, 64)),
     ("hub", 8, 40, 20, (48, 47)),
+    ("hub", 16, 5, 400, (48, 47)),      # records over a warp's slice: a CTA per unit
+    ("hub", 8, 5, 2399, (16, 16, 16)),  # records over 16 KB: ids staged, gradient read in place
     ("toy", 4, 3, 2, (6, 0)),
 ])
 def test_pull_backward_matches_unsharded(name, dim, k1, k2, batches):
