@@ -1229,6 +1229,9 @@ def profile_forward(args) -> None:
     if args.profile_forward == "onehop":
         profile_onehop(args, inp, w)
         return
+    if args.profile_forward == "pull":
+        profile_pull(args, inp, w)
+        return
     L = _lib.LIB
     k1, k2 = w.fanouts
     B, D, n = inp.B, w.dim, inp.n
@@ -1281,6 +1284,50 @@ def profile_forward(args) -> None:
     torch.cuda.synchronize()
     emit({"profile_forward": args.profile_forward, "calls": args.calls,
           "backward": args.backward, "workload": args.workload})
+
+
+def profile_pull(args, inp: Inputs, w) -> None:
+    """The owner-computed sharded backward on one GPU: `--shards` exchange
+    regions, each holding `--roots` roots of the workload sampled and
+    published as one rank would, then `--calls` pull launches for shard 0
+    of that many row shards (all regions local: the kernel's own cost
+    without NVLink)."""
+    from fusesampleagg_b200 import _lib
+
+    import ctypes
+
+    L = _lib.LIB
+    dev = inp.x.device
+    k1, k2 = w.fanouts
+    D, n, W, B = w.dim, inp.n, args.shards, args.roots
+    stream = torch.cuda.current_stream().cuda_stream
+    need = L.fsa_exchange_bytes(B, k1, k2, D)
+    ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, k1, k2, 1, 1)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    out = torch.empty((B, D), device=dev)
+    s1 = torch.empty((B, k1), dtype=torch.int32, device=dev)
+    s2 = torch.empty((B, k1, k2), dtype=torch.int32, device=dev)
+    regions = []
+    for r in range(W):
+        fr = synthetic.root_batch(n, B, seed=100 + r, device=dev)
+        _lib.check(L.fsa_sample_agg_2hop_forward(
+            inp.rowptr.data_ptr(), inp.col.data_ptr(), n, inp.col.numel(), inp.x.data_ptr(), D,
+            fr.data_ptr(), B, r * B, k1, k2, 7, out.data_ptr(), s1.data_ptr(), s2.data_ptr(),
+            ws.data_ptr(), ws_bytes, None, 0, stream), "fwd")
+        go = synthetic.features(B, D, seed=200 + r, device=dev)
+        reg = torch.empty((need,), dtype=torch.uint8, device=dev)
+        _lib.check(L.fsa_sharded_publish_2hop(reg.data_ptr(), need, go.data_ptr(), s1.data_ptr(),
+                                              s2.data_ptr(), B, D, k1, k2, stream), "publish")
+        regions.append(reg)
+    rows = -(-n // W)
+    grad = torch.zeros((rows, D), device=dev)
+    ptrs = (ctypes.c_void_p * W)(*[r.data_ptr() for r in regions])
+    for _ in range(args.calls):
+        _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
+            ptrs, need, W, 0, grad.data_ptr(), rows, n, D, k1, k2, stream), "pull")
+    torch.cuda.synchronize()
+    emit({"profile_forward": "pull", "calls": args.calls, "shards": W, "roots": B,
+          "workload": args.workload})
 
 
 def profile_onehop(args, inp: Inputs, w) -> None:
@@ -1339,10 +1386,14 @@ def main() -> None:
                    help="replicated features: all-reduce the dense feature gradient after "
                         "every backward (NCCL)")
     p.add_argument("--profile-forward",
-                   choices=["fused", "separate", "none", "persistent", "onehop"],
+                   choices=["fused", "separate", "none", "persistent", "onehop", "pull"],
                    help="run a short C-ABI call sequence for ncu instead of the benchmark")
     p.add_argument("--calls", type=int, default=3, help="calls of --profile-forward")
     p.add_argument("--fanout", type=int, default=10, help="fanout of --profile-forward onehop")
+    p.add_argument("--shards", type=int, default=8,
+                   help="exchange regions (ranks) of --profile-forward pull")
+    p.add_argument("--roots", type=int, default=2048,
+                   help="roots per exchange region of --profile-forward pull")
     p.add_argument("--backward", choices=["atomic", "sorted"], default="atomic",
                    help="backward variant of --profile-forward")
     args = p.parse_args()
