@@ -2537,6 +2537,14 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
       const float ne = static_cast<float>(nonempty);
       const float* go = reinterpret_cast<const float*>(
           (staged_grad ? static_cast<const unsigned char*>(smem_raw) : rec) + a.ids_bytes);
+      if (staged_grad) {
+        // grad_out / nonempty once per element in the staged copy (the
+        // same rounding as in (g / nonempty) / valid below)
+        float* gs = reinterpret_cast<float*>(smem_raw + a.ids_bytes);
+        for (int64_t f = tid; f < D; f += nthreads) gs[f] = gs[f] / ne;
+        __syncthreads();
+      }
+      const float pre = staged_grad ? 1.0F : ne;
       const int64_t items = static_cast<int64_t>(k1) * dvec;
       for (int64_t it = tid; it < items; it += nthreads) {
         const int i = static_cast<int>(it / dvec);
@@ -2545,7 +2553,7 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
         VecF<V> g = load_vec<V>(go + v * V);
         const float vc = static_cast<float>(valid[i]);
 #pragma unroll
-        for (int c = 0; c < V; ++c) g.v[c] = (g.v[c] / ne) / vc;
+        for (int c = 0; c < V; ++c) g.v[c] = (staged_grad ? g.v[c] : g.v[c] / pre) / vc;
         const int* rows_i = owned + i * k2;
         for (int m = 0; m < mine[i]; ++m) {
           red_add<V>(a.grad + static_cast<int64_t>(rows_i[m]) * D + v * V, g);
@@ -2596,7 +2604,7 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   int* mine = valid + k1;                                     // [k1] owned ids per slot
   int* oslot = mine + k1;                                     // [k1] slots with owned ids
   int* owned = oslot + k1;  // [k1][k2] local rows of the owned ids, slot by slot
-  const float* go = reinterpret_cast<const float*>(mem + a.ids_bytes);
+  float* go = reinterpret_cast<float*>(mem + a.ids_bytes);  // the staged gradient row
   const int dvec = static_cast<int>(a.feature_dim / V);
   const int64_t D = a.feature_dim;
   const int64_t N = a.num_nodes;
@@ -2643,18 +2651,24 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
     }
     __syncwarp();
     if (nonempty > 0 && nowned > 0) {
+      // grad_out / nonempty once per element (the staged row is this warp's
+      // copy), then / valid per owned slot: the same two roundings as
+      // (g / nonempty) / valid.
       const float ne = static_cast<float>(nonempty);
-      for (int it = lane; it < nowned * dvec; it += 32) {
-        const int t = it / dvec;
-        const int v = it - t * dvec;
+      for (int f = lane; f < static_cast<int>(D); f += 32) go[f] = go[f] / ne;
+      __syncwarp();
+      for (int t = 0; t < nowned; ++t) {
         const int i = oslot[t];
-        VecF<V> g = load_vec<V>(go + v * V);
         const float vc = static_cast<float>(valid[i]);
-#pragma unroll
-        for (int c = 0; c < V; ++c) g.v[c] = (g.v[c] / ne) / vc;
+        const int own = mine[i];
         const int* rows_i = owned + i * k2;
-        for (int m = 0; m < mine[i]; ++m) {
-          red_add<V>(a.grad + static_cast<int64_t>(rows_i[m]) * D + v * V, g);
+        for (int v = lane; v < dvec; v += 32) {
+          VecF<V> g = load_vec<V>(go + v * V);
+#pragma unroll
+          for (int c = 0; c < V; ++c) g.v[c] = g.v[c] / vc;
+          for (int m = 0; m < own; ++m) {
+            red_add<V>(a.grad + static_cast<int64_t>(rows_i[m]) * D + v * V, g);
+          }
         }
       }
     }
