@@ -22,7 +22,9 @@ each rank takes its contiguous 1024-root slice of a global batch with
 ``batch_offset = rank * 1024`` (ids identical to a single-GPU run of the
 global batch); no collective on the data path (weak scaling).  After the
 main measurement, on 2+ GPUs: the same step followed by the NCCL all-reduce
-of the dense feature gradient (`replicated_allreduce`), the row-sharded mode
+of the dense feature gradient (`replicated_allreduce`), the same gradient
+summed through exchange regions instead (`replicated_exchange`), the
+row-sharded mode
 checked bit for bit against the replicated op and timed (`sharded`), and the
 100M-node configuration (`c5`; replicated on one GPU, row-sharded on 2+).
 
@@ -817,6 +819,77 @@ def allreduce_leg(w, inp: Inputs, args, dist: Dist, base_ms_per_step: float) -> 
     }
 
 
+def exchange_leg(w, inp: Inputs, args, dist: Dist, base_ms_per_step: float) -> dict:
+    """The replicated step whose backward leaves every rank with the whole
+    global batch's feature gradient through exchange regions
+    (`sharding.GradientExchange`: every rank publishes its saved ids and
+    upstream gradient, every rank adds all ranks' contributions) instead of
+    the NCCL all-reduce of the dense gradient.  Checked once against the
+    all-reduced gradient (rtol 1e-5 / atol 1e-6), then timed like the main
+    step, max over ranks.  Every rank takes the same collective steps."""
+    import torch.distributed as tdist
+
+    import fusesampleagg_b200 as fsa
+    from fusesampleagg_b200 import sharding
+
+    k1, k2 = w.fanouts
+    ex = sharding.GradientExchange(inp.n, w.dim,
+                                   sharding.exchange_bytes(w.batch, k1, k2, w.dim),
+                                   device=inp.x.device)
+    x = inp.x
+    x.grad = None
+    fsa.fused_sample_agg_2hop(inp.rowptr, inp.col, x, inp.frontiers[0], k1, k2,
+                              replay_seed=inp.seeds[0], batch_offset=inp.offset
+                              ).backward(inp.grad_out)
+    want = x.grad
+    x.grad = None
+    tdist.all_reduce(want)
+    sharding.fused_sample_agg_2hop_exchange(inp.rowptr, inp.col, x, inp.frontiers[0], k1, k2,
+                                            replay_seed=inp.seeds[0], batch_offset=inp.offset,
+                                            exchange=ex).backward(inp.grad_out)
+    torch.cuda.synchronize()
+    err = (x.grad - want).abs()
+    ok = bool((err <= 1e-6 + 1e-5 * want.abs()).all())
+    max_err = float(err.max()) if err.numel() else 0.0
+    x.grad = None
+    del want, err
+    torch.cuda.empty_cache()
+    flag = torch.tensor([float(ok)], device="cuda")
+    tdist.all_reduce(flag, op=tdist.ReduceOp.MIN)
+
+    class Api:
+        @staticmethod
+        def fused_sample_agg_2hop(rowptr, col, x, frontier, f1, f2, replay_seed=1234,
+                                  batch_offset=0):
+            return sharding.fused_sample_agg_2hop_exchange(rowptr, col, x, frontier, f1, f2,
+                                                           replay_seed, batch_offset,
+                                                           exchange=ex)
+
+    launches0 = fsa.launch_count()
+    ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
+    launches = (fsa.launch_count() - launches0) * args.steps // (args.steps + args.warmup)
+    ex.close()
+    units = w.batch * dist.world * args.steps
+    per_step = ms / args.steps
+    return {
+        "value": units / (ms / 1000.0),
+        "unit": "roots/s",
+        "ms_per_step": per_step,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "gpu_launches": launches,
+        "exchange_ms_per_step": max(per_step - base_ms_per_step, 0.0),
+        "grad_matches_allreduce": bool(flag[0].item() == 1.0),
+        "grad_check": "every rank's gradient vs the NCCL-all-reduced per-rank gradients, "
+                      "rtol 1e-5 / atol 1e-6",
+        "grad_max_abs_err_rank0": max_err,
+        "mode": ("replicated features; the backward publishes this rank's saved ids and "
+                 "upstream gradient in an exchange region mapped into every peer (CUDA IPC) and "
+                 "adds every rank's contributions into this rank's gradient after a one-float "
+                 "NCCL all-reduce: the all-reduced gradient without moving the dense N x D"),
+    }
+
+
 def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     """The row-sharded mode on the same global batch (2+ GPUs): this rank's
     ids and outputs against the replicated op's for the same slice, bit for
@@ -1194,6 +1267,7 @@ def run(args) -> None:
     if args.impl == "ours" and feats is None and not args.allreduce_grad:
         if world >= 2 and not args.no_allreduce_leg:
             result["replicated_allreduce"] = allreduce_leg(w, inp, args, dist, ms / args.steps)
+            result["replicated_exchange"] = exchange_leg(w, inp, args, dist, ms / args.steps)
         if world >= 2 and not args.no_sharded_leg:
             result["sharded"] = sharded_leg(w, inp, args, dist)
         if not args.no_c5 and args.workload != "c5_2hop_100m":

@@ -58,6 +58,52 @@ def shard_span(num_nodes: int, rank: int, world: int) -> tuple[int, int]:
     return start, min(start + rows, num_nodes)
 
 
+def _ipc_share(tensors, group, device: int, stand_in: int):
+    """Collective: exports this rank's `tensors` (entries may be None or
+    empty) as CUDA IPC handles, gathers every rank's and maps the peers'
+    allocations once into `device`'s address space.  Returns, per tensor,
+    the list of every rank's pointer valid in this process (`stand_in` for
+    a rank's None or empty tensor), and the {handle: base} mappings to close."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    from . import _lib
+
+    L = _lib.LIB
+
+    def export(t):
+        if t is None or t.numel() == 0:
+            return None
+        h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        off = ctypes.c_uint64(0)
+        _lib.check(L.fsa_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "fsa_ipc_export")
+        return h.raw, off.value
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    shared = [None] * world
+    dist.all_gather_object(shared, [export(t) for t in tensors], group=group)
+    mapped = {}
+    out = [[] for _ in tensors]
+    for r, entries in enumerate(shared):
+        for k, e in enumerate(entries):
+            if r == rank:
+                t = tensors[k]
+                out[k].append(t.data_ptr() if t is not None and t.numel() > 0 else stand_in)
+                continue
+            if e is None:
+                out[k].append(stand_in)
+                continue
+            handle, off = e
+            if handle not in mapped:
+                base = ctypes.c_void_p()
+                _lib.check(L.fsa_ipc_open(handle, device, ctypes.byref(base)), "fsa_ipc_open")
+                mapped[handle] = base.value
+            out[k].append(mapped[handle] + off)
+    return out, mapped
+
+
 class ShardedFeatures:
     """A float32 feature table block-partitioned by row over the ranks of a
     NCCL process group, one GPU per rank, plus its gradient shards.
@@ -114,44 +160,12 @@ class ShardedFeatures:
         self.pull = self.exchange is not None
         self._flag = torch.zeros(1, device=self.local.device)
         self._device = self.local.device.index
-        L = _lib.LIB
-
-        def export(t):
-            if t.numel() == 0:
-                return None
-            h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
-            off = ctypes.c_uint64(0)
-            _lib.check(L.fsa_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "fsa_ipc_export")
-            return h.raw, off.value
-
-        shared = [None] * self.world
-        mine = (export(self.local), export(self.grad),
-                export(self.exchange) if self.exchange is not None else None)
-        dist.all_gather_object(shared, mine, group=group)
-        # Map every peer allocation once, into this device's address space.
-        self._mapped = {}
-        xs, gs, es = [], [], []
-        for r, (xe, ge, ee) in enumerate(shared):
-            if r == self.rank:
-                xs.append(self.local.data_ptr())
-                gs.append(self.grad.data_ptr())
-                es.append(self.exchange.data_ptr() if self.exchange is not None else 0)
-                continue
-            for e, out in ((xe, xs), (ge, gs), (ee, es)):
-                if e is None:  # an empty trailing shard (or no exchange): any aligned base
-                    out.append(self.local.data_ptr())
-                    continue
-                handle, off = e
-                if handle not in self._mapped:
-                    base = ctypes.c_void_p()
-                    _lib.check(L.fsa_ipc_open(handle, self._device, ctypes.byref(base)),
-                               "fsa_ipc_open")
-                    self._mapped[handle] = base.value
-                out.append(self._mapped[handle] + off)
-        ptrs = ctypes.c_void_p * self.world
-        self.x_ptrs = ptrs(*xs)
-        self.grad_ptrs = ptrs(*gs)
-        self.exchange_ptrs = ptrs(*es) if self.exchange is not None else None
+        ptrs, self._mapped = _ipc_share(
+            [self.local, self.grad, self.exchange], group, self._device, self.local.data_ptr())
+        arr = ctypes.c_void_p * self.world
+        self.x_ptrs = arr(*ptrs[0])
+        self.grad_ptrs = arr(*ptrs[1])
+        self.exchange_ptrs = arr(*ptrs[2]) if self.exchange is not None else None
 
     def device_barrier(self) -> None:
         """Orders the GPUs: the current stream of every rank waits until every
@@ -315,3 +329,156 @@ def fused_sample_agg_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier,
     """
     return _Sharded2HopFn.apply(feats.local, rowptr, col, frontier, fanout1, fanout2,
                                 replay_seed, batch_offset, feats)
+
+
+# ---------------------------------------------------------------------------
+# Replicated features, gradient summed over the ranks by exchange
+# ---------------------------------------------------------------------------
+
+class GradientExchange:
+    """Exchange regions for replicated features: the alternative to an NCCL
+    all-reduce of the dense N x D feature gradient after every backward.
+
+    Every rank publishes its step's saved ids and upstream gradient in its
+    region (mapped into every peer over CUDA IPC); after a device barrier
+    every rank adds every rank's contributions into its own zero-filled
+    gradient (the owner-computed backward with one shard covering all rows).
+    Every rank then holds the gradient of the whole global batch -- the
+    all-reduced gradient, up to the order of the fp32 additions -- while
+    NVLink carries (W - 1) * B * (4 (f1 + f1 f2) + 4 D) bytes per rank
+    instead of the all-reduce's ~2 * 4 N D.  Construction and `close()` are
+    collective.
+    """
+
+    def __init__(self, num_nodes: int, dim: int, exchange_bytes: int, device=None, group=None):
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _lib.MAX_SHARDS:
+            raise ValueError(f"at most {_lib.MAX_SHARDS} ranks")
+        if num_nodes < 1 or num_nodes > 0x7FFFFFFF or dim < 0 or exchange_bytes < 256:
+            raise ValueError("num_nodes must be in [1, 2^31), dim >= 0, exchange_bytes >= 256")
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        self.num_nodes, self.dim, self.exchange_bytes = int(num_nodes), int(dim), int(exchange_bytes)
+        self.exchange = torch.empty((self.exchange_bytes,), dtype=torch.uint8, device=dev)
+        self._flag = torch.zeros(1, device=dev)
+        self._device = dev.index
+        import ctypes
+
+        ptrs, self._mapped = _ipc_share([self.exchange], group, self._device,
+                                        self.exchange.data_ptr())
+        self.exchange_ptrs = (ctypes.c_void_p * self.world)(*ptrs[0])
+
+    def device_barrier(self) -> None:
+        """NCCL all-reduce of one float on the current stream (no host sync)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        """Unmaps the peers' regions (collective)."""
+        import torch.distributed as dist
+
+        from . import _lib
+
+        torch.cuda.synchronize(self.exchange.device)
+        dist.barrier(group=self.group)
+        for base in self._mapped.values():
+            _lib.check(_lib.LIB.fsa_ipc_close(base, self._device), "fsa_ipc_close")
+        self._mapped.clear()
+        self.exchange_ptrs = None
+        dist.barrier(group=self.group)
+
+
+class _Exchange2HopFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, rowptr, col, frontier, fanout1, fanout2, replay_seed, batch_offset, ex):
+        from . import _as_int64, _as_seed, _check_fanout_2hop, _check_offset
+        from . import _check_python_inputs, _DeviceGuard, _lib, _stream_handle
+
+        L = _lib.LIB
+        _check_python_inputs(rowptr, col, x, frontier)
+        fanout1 = _as_int64(fanout1, "fanout1")
+        fanout2 = _as_int64(fanout2, "fanout2")
+        _check_fanout_2hop(fanout1, fanout2)
+        seed = _as_seed(replay_seed)
+        off = _check_offset(batch_offset)
+        rowptr, col, frontier = rowptr.contiguous(), col.contiguous(), frontier.contiguous()
+        xc = x.detach().contiguous()
+        if xc.dim() != 2 or rowptr.numel() != xc.size(0) + 1:
+            raise RuntimeError("x must be [N, D] with rowptr of N + 1 entries")
+        N, D = xc.shape
+        B = frontier.numel()
+        if N != ex.num_nodes or D != ex.dim:
+            raise RuntimeError("x must be [num_nodes, dim] of the GradientExchange")
+        dev = xc.device
+        with _DeviceGuard(dev):
+            out = torch.empty((B, D), dtype=torch.float32, device=dev)
+            s1 = torch.full((B, fanout1), -1, dtype=torch.int32, device=dev)
+            s2 = torch.full((B, fanout1, fanout2), -1, dtype=torch.int32, device=dev)
+            grad = torch.empty_like(xc)
+            ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, 1, 1)
+            ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+            _lib.check(L.fsa_sample_agg_2hop_forward(
+                rowptr.data_ptr(), col.data_ptr(), N, col.numel(), xc.data_ptr(), D,
+                frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(),
+                s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, grad.data_ptr(),
+                grad.numel(), _stream_handle(dev)), "fsa_sample_agg_2hop_forward")
+            if fanout1 == 0 or fanout2 == 0:
+                out.zero_()  # nothing sampled (fuseop/binding.cpp:183-185)
+        ctx.save_for_backward(s1, s2)
+        ctx.grad = grad
+        ctx.ex = ex
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        from . import _DeviceGuard, _lib, _stream_handle
+
+        ex = ctx.ex
+        s1, s2 = ctx.saved_tensors
+        grad = ctx.grad
+        ctx.grad = ctx.ex = None
+        g = grad_out.contiguous()
+        B, D = g.shape
+        k1, k2 = s1.size(1), s2.size(2)
+        L = _lib.LIB
+        need = int(L.fsa_exchange_bytes(B, k1, k2, D))
+        if need == 0 or need > ex.exchange_bytes:
+            raise RuntimeError(f"a backward of {B} roots at fanouts ({k1}, {k2}) needs an exchange "
+                               f"region of {need} bytes; this GradientExchange has "
+                               f"{ex.exchange_bytes}")
+        with _DeviceGuard(g.device):
+            stream = _stream_handle(g.device)
+            _lib.check(L.fsa_sharded_publish_2hop(ex.exchange.data_ptr(), ex.exchange_bytes,
+                                                  g.data_ptr(), s1.data_ptr(), s2.data_ptr(), B,
+                                                  D, k1, k2, stream), "fsa_sharded_publish_2hop")
+            ex.device_barrier()  # every rank's region holds this step's records
+            # one shard of all N rows: every contribution of every rank is this rank's
+            _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
+                ex.exchange_ptrs, ex.exchange_bytes, ex.world, 0, grad.data_ptr(), ex.num_nodes,
+                ex.num_nodes, D, k1, k2, stream), "fsa_sample_agg_2hop_backward_sharded_pull")
+            ex.device_barrier()  # every rank has read the regions before they are rewritten
+        return (grad,) + (None,) * 8
+
+
+def fused_sample_agg_2hop_exchange(rowptr, col, x, frontier, fanout1, fanout2,
+                                   replay_seed=1234, batch_offset=0, *, exchange):
+    """``fused_sample_agg_2hop`` on replicated features whose backward gives
+    every rank the feature gradient of the whole global batch (what an
+    all-reduce of the per-rank gradients gives) through `exchange`, a
+    `GradientExchange`.  The ids and outputs are those of
+    ``fused_sample_agg_2hop`` with the same `batch_offset`.  Collective
+    when training: every rank calls forward and backward together.  Without
+    ``x.requires_grad`` this is the plain op."""
+    from . import fused_sample_agg_2hop
+
+    if not x.requires_grad:
+        return fused_sample_agg_2hop(rowptr, col, x, frontier, fanout1, fanout2, replay_seed,
+                                     batch_offset=batch_offset)
+    return _Exchange2HopFn.apply(x, rowptr, col, frontier, fanout1, fanout2, replay_seed,
+                                 batch_offset, exchange)

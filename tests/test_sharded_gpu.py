@@ -110,3 +110,66 @@ def test_sharded_two_gpus_match_unsharded(dim, fans, pull):
         mp.spawn(_worker, args=(world, _free_port(), dim, fans, pull, results), nprocs=world,
                  join=True)
         assert dict(results) == {0: True, 1: True}
+
+
+def _exchange_worker(rank, world, port, results):
+    import torch.distributed as dist
+
+    import fusesampleagg_b200 as fsa
+    from fusesampleagg_b200 import synthetic
+    from tests.golden import cases as C
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    ex = None
+    try:
+        g = C.powerlaw_graph()
+        rp, cl = g.rowptr.to(dev), g.col.to(dev)
+        n, dim, (k1, k2) = g.num_nodes, 48, (15, 10)
+        x = synthetic.features(n, dim, seed=1, device=dev)
+        roots = synthetic.root_batch(n, 256, seed=4, device=dev)
+        mine, off = sharding.local_roots(roots, rank, world)
+        ex = sharding.GradientExchange(n, dim, sharding.exchange_bytes(-(-256 // world), k1, k2,
+                                                                        dim), device=dev)
+        ok = True
+        for step in range(2):
+            go = synthetic.features(mine.numel(), dim, seed=20 + 2 * rank + step, device=dev)
+            xe = x.clone().requires_grad_(True)
+            out = sharding.fused_sample_agg_2hop_exchange(rp, cl, xe, mine, k1, k2,
+                                                          replay_seed=step, batch_offset=off,
+                                                          exchange=ex)
+            out.backward(go)
+            xr = x.clone().requires_grad_(True)
+            ref = fsa.fused_sample_agg_2hop(rp, cl, xr, mine, k1, k2, replay_seed=step,
+                                            batch_offset=off)
+            ref.backward(go)
+            full = xr.grad.clone()
+            dist.all_reduce(full)
+            torch.cuda.synchronize()
+            ok &= torch.equal(out.view(torch.int32), ref.detach().view(torch.int32))
+            ok &= torch.allclose(xe.grad, full, rtol=RTOL, atol=ATOL)
+        results[rank] = bool(ok)
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_gradient_exchange_two_gpus_equals_allreduce():
+    """Replicated features: the exchange backward leaves every rank with the
+    all-reduced gradient of the per-rank gradients."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.spawn(_exchange_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        assert dict(results) == {0: True, 1: True}
+

@@ -94,3 +94,33 @@ def test_pull_backward_matches_unsharded(name, dim, k1, k2, batches):
     got, want = run(name, dim, k1, k2, batches, world)
     torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
     assert _lib.device_status(torch.cuda.current_device(), reset=True) == 0
+
+
+def test_one_shard_of_all_rows_sums_every_rank():
+    """The replicated-feature exchange (GradientExchange): each rank pulls
+    with one shard covering all N rows, so its gradient is the sum over all
+    ranks' roots -- the all-reduced gradient."""
+    name, dim, k1, k2, batches = "powerlaw", 64, 15, 10, (128, 128, 128)
+    g, _, _ = graph(name)
+    n = g.num_nodes
+    world = len(batches)
+    ranks = []
+    for r, batch in enumerate(batches):
+        s1, s2 = sample(name, dim, k1, k2, batch, 60 + r, r * batch)
+        ranks.append((s1, s2, synthetic.features(batch, dim, seed=9 + r, device="cuda")))
+    need = L.fsa_exchange_bytes(max(batches), k1, k2, dim)
+    regions = [torch.empty((need,), dtype=torch.uint8, device="cuda") for _ in range(world)]
+    for (s1, s2, go), reg, b in zip(ranks, regions, batches):
+        _lib.check(L.fsa_sharded_publish_2hop(reg.data_ptr(), need, go.data_ptr(), s1.data_ptr(),
+                                              s2.data_ptr(), b, dim, k1, k2, stream()), "publish")
+    ptrs = (ctypes.c_void_p * world)(*[r.data_ptr() for r in regions])
+    got = torch.zeros(n, dim, device="cuda")
+    _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
+        ptrs, need, world, 0, got.data_ptr(), n, n, dim, k1, k2, stream()), "pull")
+    want = torch.zeros(n, dim, device="cuda")
+    for (s1, s2, go), b in zip(ranks, batches):
+        _lib.check(L.fsa_sample_agg_2hop_backward(go.data_ptr(), s1.data_ptr(), s2.data_ptr(), b,
+                                                  dim, k1, k2, want.data_ptr(), n, stream()),
+                   "backward")
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
