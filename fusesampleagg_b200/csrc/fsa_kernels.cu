@@ -2496,9 +2496,8 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   const int64_t D = a.feature_dim;
   const int64_t dvec = D / V;
   const int64_t N = a.num_nodes;
-  const uint32_t rows = static_cast<uint32_t>(a.shard_rows);
-  const uint32_t me = static_cast<uint32_t>(a.shard);
-  const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;
+  const uint64_t rows = static_cast<uint64_t>(a.shard_rows);
+  const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;  // this shard: [lo, lo + rows)
   const int64_t units = a.cap_roots * a.num_shards;
   for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
     const int s = static_cast<int>(u % a.num_shards);
@@ -2520,7 +2519,7 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
         ++cnt;
         if (leaf >= N) {
           flag_status(FSA_STATUS_BAD_NEIGHBOR);
-        } else if (static_cast<uint32_t>(leaf) / rows == me) {
+        } else if (static_cast<uint64_t>(leaf - lo) < rows) {
           owned[i * k2 + own++] = static_cast<int>(leaf - lo);
         }
       }
@@ -2608,9 +2607,8 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   const int dvec = static_cast<int>(a.feature_dim / V);
   const int64_t D = a.feature_dim;
   const int64_t N = a.num_nodes;
-  const uint32_t rows = static_cast<uint32_t>(a.shard_rows);
-  const uint32_t me = static_cast<uint32_t>(a.shard);
-  const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;
+  const uint64_t rows = static_cast<uint64_t>(a.shard_rows);
+  const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;  // this shard: [lo, lo + rows)
   const int64_t units = a.cap_roots * a.num_shards;
   for (int64_t u = static_cast<int64_t>(blockIdx.x) * nwarps + warp; u < units;
        u += static_cast<int64_t>(gridDim.x) * nwarps) {
@@ -2623,27 +2621,44 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
       int4* dst = reinterpret_cast<int4*>(mem);
       for (int q = lane; q < static_cast<int>(a.staged_bytes / 16); q += 32) dst[q] = src[q];
     }
+    for (int i = lane; i < k1; i += 32) {
+      valid[i] = 0;
+      mine[i] = 0;
+    }
+    __syncwarp();
+    // every lane takes entries lane, lane + 32, ...: (slot, position)
+    // advance by (32 / k2, 32 % k2) with a carry; counts and owned rows by
+    // shared-memory atomics (the order of a slot's owned rows is free)
+    {
+      const int di = 32 / k2;
+      const int dj = 32 - di * k2;
+      int i = lane / k2;
+      int j = lane - i * k2;
+      for (int e = lane; e < k1 * k2; e += 32) {
+        const int32_t leaf = ids[k1 + e];
+        if (leaf >= 0) {
+          atomicAdd(&valid[i], 1);
+          if (leaf >= N) {
+            flag_status(FSA_STATUS_BAD_NEIGHBOR);
+          } else if (static_cast<uint64_t>(leaf - lo) < rows) {
+            owned[i * k2 + atomicAdd(&mine[i], 1)] = static_cast<int>(leaf - lo);
+          }
+        }
+        i += di;
+        j += dj;
+        if (j >= k2) {
+          j -= k2;
+          ++i;
+        }
+      }
+    }
     __syncwarp();
     int nonempty = 0;
     int nowned = 0;  // slots with owned ids, listed in oslot
     for (int i0 = 0; i0 < k1; i0 += 32) {
       const int i = i0 + lane;
-      int cnt = 0;
-      int own = 0;
-      if (i < k1) {
-        for (int j = 0; j < k2; ++j) {
-          const int32_t leaf = ids[k1 + i * k2 + j];
-          if (leaf < 0) continue;
-          ++cnt;
-          if (leaf >= N) {
-            flag_status(FSA_STATUS_BAD_NEIGHBOR);
-          } else if (static_cast<uint32_t>(leaf) / rows == me) {
-            owned[i * k2 + own++] = static_cast<int>(leaf - lo);
-          }
-        }
-        valid[i] = cnt;
-        mine[i] = own;
-      }
+      const int cnt = i < k1 ? valid[i] : 0;
+      const int own = i < k1 ? mine[i] : 0;
       nonempty += __popc(__ballot_sync(0xffffffffU, i < k1 && ids[i] >= 0 && cnt > 0));
       const unsigned has = __ballot_sync(0xffffffffU, own > 0);
       if (own > 0) oslot[nowned + __popc(has & ((1U << lane) - 1U))] = i;
