@@ -2399,7 +2399,7 @@ namespace {
 constexpr int64_t kExchangeHeader = 256;
 constexpr int kThreadsPublish = 256;
 constexpr int kThreadsPull = 128;
-constexpr int kPullCtasPerSm = 16;
+constexpr int kPullCtasPerSm = 12;
 
 // Bytes of one root's record: samples1 and samples2 (int32), padded to 16
 // bytes, then the upstream gradient row (float), padded to 16 bytes.
@@ -2498,10 +2498,20 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   const int64_t N = a.num_nodes;
   const uint64_t rows = static_cast<uint64_t>(a.shard_rows);
   const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;  // this shard: [lo, lo + rows)
-  const int64_t units = a.cap_roots * a.num_shards;
-  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-    const int s = static_cast<int>(u % a.num_shards);
-    const int64_t b = u / a.num_shards;
+  // unit u = b * num_shards + s, walked with a stride of gridDim.x units:
+  // (b, s) advance with a carry instead of a 64-bit division per unit
+  const int W = a.num_shards;
+  const int64_t step = gridDim.x;
+  const int64_t db = step / W;
+  const int ds = static_cast<int>(step - db * W);
+  int64_t b = blockIdx.x / W;
+  int s = static_cast<int>(blockIdx.x - b * W);
+  for (; b < a.cap_roots; b += db, s += ds) {
+    if (s >= W) {
+      s -= W;
+      ++b;
+      if (b >= a.cap_roots) break;
+    }
     if (b >= s_roots[s]) continue;  // the same for the whole CTA
     const unsigned char* rec = a.regions[s] + kExchangeHeader + b * a.stride;
     {
@@ -2544,11 +2554,11 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
         __syncthreads();
       }
       const float pre = staged_grad ? 1.0F : ne;
-      const int64_t items = static_cast<int64_t>(k1) * dvec;
-      for (int64_t it = tid; it < items; it += nthreads) {
-        const int i = static_cast<int>(it / dvec);
+      const int dv = static_cast<int>(dvec);  // k1 * dvec < 2^31 (checked on the host)
+      for (int it = tid; it < k1 * dv; it += nthreads) {
+        const int i = it / dv;
         if (mine[i] == 0) continue;
-        const int64_t v = it - static_cast<int64_t>(i) * dvec;
+        const int v = it - i * dv;
         VecF<V> g = load_vec<V>(go + v * V);
         const float vc = static_cast<float>(valid[i]);
 #pragma unroll
@@ -2609,11 +2619,21 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   const int64_t N = a.num_nodes;
   const uint64_t rows = static_cast<uint64_t>(a.shard_rows);
   const int64_t lo = static_cast<int64_t>(a.shard) * a.shard_rows;  // this shard: [lo, lo + rows)
-  const int64_t units = a.cap_roots * a.num_shards;
-  for (int64_t u = static_cast<int64_t>(blockIdx.x) * nwarps + warp; u < units;
-       u += static_cast<int64_t>(gridDim.x) * nwarps) {
-    const int s = static_cast<int>(u % a.num_shards);
-    const int64_t b = u / a.num_shards;
+  // unit u = b * num_shards + s, walked with a stride of gridDim.x * nwarps
+  // units: (b, s) advance with a carry instead of a 64-bit division per unit
+  const int W = a.num_shards;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * nwarps;
+  const int64_t db = step / W;
+  const int ds = static_cast<int>(step - db * W);
+  const int64_t u0 = static_cast<int64_t>(blockIdx.x) * nwarps + warp;
+  int64_t b = u0 / W;
+  int s = static_cast<int>(u0 - b * W);
+  for (; b < a.cap_roots; b += db, s += ds) {
+    if (s >= W) {
+      s -= W;
+      ++b;
+      if (b >= a.cap_roots) break;
+    }
     if (b >= s_roots[s]) continue;  // the same for the whole warp
     {
       const int4* src =
@@ -2755,6 +2775,8 @@ int fsa_sample_agg_2hop_backward_sharded_pull(const void* const* exchanges,
   }
   if (fanout1 == 0 || fanout2 == 0 || feature_dim == 0) return FSA_OK;
   if (grad_shard == nullptr || !aligned(grad_shard, 4)) return FSA_ERR_INVALID_ARGUMENT;
+  // the kernels index a root's (slot, element) items in 32 bits
+  if (static_cast<int64_t>(fanout1) * feature_dim >= 0x7fffffffLL) return FSA_ERR_INVALID_ARGUMENT;
   const int64_t stride = exchange_root_bytes(fanout1, fanout2, feature_dim);
   pa.cap_roots = (static_cast<int64_t>(exchange_bytes) - kExchangeHeader) / stride;
   if (pa.cap_roots == 0) return FSA_OK;
