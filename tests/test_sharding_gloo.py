@@ -101,3 +101,16 @@ def test_failed_rank_surfaces_as_error(tmp_path):
     with pytest.raises(Exception):
         mp.start_processes(_worker, args=(2, free_port(), str(tmp_path), 1), nprocs=2,
                            start_method="spawn")
+
+
+def test_exchange_bytes_helper():
+    """Region size of the owner-computed backward / gradient exchange: the C
+    ABI's layout; invalid sizes raise before anything is allocated."""
+    from fusesampleagg_b200 import sharding
+
+    assert sharding.exchange_bytes(1024, 15, 10, 100) == 256 + 1024 * (672 + 400)
+    assert sharding.exchange_bytes(0, 15, 10, 100) == 256
+    with pytest.raises(ValueError):
+        sharding.exchange_bytes(-1, 15, 10, 100)
+    with pytest.raises(ValueError):
+        sharding.exchange_bytes(8, 5, 2400, 16)  # over the 12000-entry limit
