@@ -362,7 +362,11 @@ class GradientExchange:
             raise ValueError(f"at most {_lib.MAX_SHARDS} ranks")
         if num_nodes < 1 or num_nodes > 0x7FFFFFFF or dim < 0 or exchange_bytes < 256:
             raise ValueError("num_nodes must be in [1, 2^31), dim >= 0, exchange_bytes >= 256")
-        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        dev = torch.device("cuda") if device is None else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("the exchange region lives on a CUDA device")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         self.num_nodes, self.dim, self.exchange_bytes = int(num_nodes), int(dim), int(exchange_bytes)
         self.exchange = torch.empty((self.exchange_bytes,), dtype=torch.uint8, device=dev)
         self._flag = torch.zeros(1, device=dev)
