@@ -24,14 +24,14 @@ global batch); no collective on the data path (weak scaling).  After the
 main measurement, on 2+ GPUs: the same step followed by the NCCL all-reduce
 of the dense feature gradient (`replicated_allreduce`), the same gradient
 summed through exchange regions instead (`replicated_exchange`), the
-row-sharded mode
-checked bit for bit against the replicated op and timed (`sharded`), and the
-100M-node configuration (`c5`; replicated on one GPU, row-sharded on 2+).
+row-sharded mode checked bit for bit against the replicated op and timed
+(`sharded`), and the 100M-node configuration (`c5`; replicated on one GPU,
+row-sharded on 2+).
 
 ``--impl reference`` runs the reference's own CUDA op (built from its
 sources into oracle/_ref) on the same workload through its public API, on
-every rank (each rank times its own 1024 roots).  The CPU baseline (rank 0, N=1) is the sequential C oracle on a
-bounded sample of the same workload.
+every rank (each rank times its own 1024 roots).  The CPU baseline (rank 0,
+N=1) is the sequential C oracle on a bounded sample of the same workload.
 """
 
 from __future__ import annotations
