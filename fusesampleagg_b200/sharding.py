@@ -419,6 +419,8 @@ class _Exchange2HopFn(torch.autograd.Function):
         B = frontier.numel()
         if N != ex.num_nodes or D != ex.dim:
             raise RuntimeError("x must be [num_nodes, dim] of the GradientExchange")
+        if xc.device != ex.exchange.device:
+            raise RuntimeError("x must be on the GradientExchange's device")
         dev = xc.device
         with _DeviceGuard(dev):
             out = torch.empty((B, D), dtype=torch.float32, device=dev)
