@@ -959,6 +959,22 @@ def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
     feats.pull = False
     push_ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
     feats.pull = True
+    # the same steps with the gradient shard kept across steps: each forward
+    # clears the rows the previous backward listed instead of zero-filling
+    # the shard; then one step's shard against a freshly filled one
+    feats.persistent = True
+    pers_ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
+    j = (args.warmup + args.steps) % len(inp.frontiers)
+    step_j = make_step(Api, w, inp, batch_offset=True)
+    step_j(j)
+    kept = feats.grad.clone()
+    feats.persistent = False
+    step_j(j)
+    torch.cuda.synchronize()
+    pers_ok = bool(torch.isclose(kept, feats.grad, rtol=1e-5, atol=1e-6).all())
+    del kept
+    pflag = torch.tensor([float(pers_ok)], device="cuda")
+    tdist.all_reduce(pflag, op=tdist.ReduceOp.MIN)
     feats.close()
     del feats
     torch.cuda.empty_cache()
@@ -979,6 +995,12 @@ def sharded_leg(w, inp: Inputs, args, dist: Dist) -> dict:
         "gpu_launches": launches,
         "push": {"value": units / (push_ms / 1000.0), "ms_per_step": push_ms / args.steps,
                  "backward": "one red.add per remote contribution over NVLink"},
+        "persistent_grad": {"value": units / (pers_ms / 1000.0),
+                            "ms_per_step": pers_ms / args.steps,
+                            "matches_fresh_gradient": bool(pflag[0].item() == 1.0),
+                            "clear": ("rows the previous owner-computed backward listed, zeroed "
+                                      "inside the sampling kernel instead of the shard's dense "
+                                      "fill (ShardedFeatures(persistent=True))")},
         "mode": ("feature rows and their gradient block-sharded over the GPUs: remote rows "
                  "read over NVLink through peer pointers (plain loads, no multicast); backward "
                  "computed by the owners: every rank publishes its saved ids and upstream "
@@ -1029,6 +1051,13 @@ def c5_leg(args, dist: Dist, dev) -> dict:
         push = {"value": w5.batch * dist.world * steps / (push_ms / 1000.0),
                 "ms_per_step": push_ms / steps,
                 "backward": "one red.add per remote contribution over NVLink"}
+        # the gradient shards kept across steps, touched rows cleared
+        feats.persistent = True
+        pers_ms, _ = timed(make_step(step_api, w5, inp, batch_offset=True), steps, warmup, dist)
+        feats.persistent = False
+        persistent = {"value": w5.batch * dist.world * steps / (pers_ms / 1000.0),
+                      "ms_per_step": pers_ms / steps,
+                      "clear": "rows the previous backward listed, inside the sampling kernel"}
         feats.close()
     units = w5.batch * dist.world * steps
     out = {
@@ -1413,7 +1442,7 @@ def profile_pull(args, inp: Inputs, w) -> None:
     ptrs = (ctypes.c_void_p * W)(*[r.data_ptr() for r in regions])
     for _ in range(args.calls):
         _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
-            ptrs, need, W, 0, grad.data_ptr(), rows, n, D, k1, k2, stream), "pull")
+            ptrs, need, W, 0, grad.data_ptr(), rows, n, D, k1, k2, None, 0, stream), "pull")
     torch.cuda.synchronize()
     emit({"profile_forward": "pull", "calls": args.calls, "shards": W, "roots": B,
           "workload": args.workload})

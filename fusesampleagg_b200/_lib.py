@@ -64,7 +64,10 @@ SIGNATURES = {
                                         _p]),
     "fsa_sample_agg_2hop_backward_sharded_pull": (
         _int, [ctypes.POINTER(_p), ctypes.c_size_t, _i32, _i32, _p, _i64, _i64, _i64, _i32, _i32,
-               _p]),
+               _p, _i64, _p]),
+    "fsa_sample_agg_2hop_forward_sharded_zero_rows": (
+        _int, [_p, _p, _i64, _i64, ctypes.POINTER(_p), _i64, _i32, _i64, _p, _i64, _i64, _i32,
+               _i32, _u64, _p, _p, _p, _p, ctypes.c_size_t, _p, _i64, _p, _i64, _p]),
     "fsa_fill_zero_f32": (_int, [_p, _i64, _p]),
     "fsa_zero_rows_f32": (_int, [_p, _i64, _i64, _p, _i64, _p]),
     "fsa_phase_timing": (_int, [_int]),

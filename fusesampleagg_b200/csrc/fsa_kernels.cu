@@ -1760,7 +1760,8 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
                         int32_t* samples1, int32_t* samples2, void* workspace,
                         size_t workspace_bytes, float* zero_fill, int64_t zero_count,
                         void* stream, const RowShards* xs, float* zero_table = nullptr,
-                        const int32_t* zero_rows = nullptr, int64_t zero_rows_count = 0) {
+                        const int32_t* zero_rows = nullptr, int64_t zero_rows_count = 0,
+                        int64_t zero_table_rows = -1) {
   const int arg_status =
       check_forward_2hop_args(rowptr, col, num_nodes, num_edges, x, feature_dim, frontier,
                               batch_size, batch_offset, fanout1, fanout2, out, zero_fill,
@@ -1777,14 +1778,15 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
   // float4 vectors (at most 32 of them) and no dense fill rides along, else
   // with the stand-alone row kernel before the forward.
   float4* ztable4 = nullptr;
+  const int64_t ztable_rows = zero_table_rows >= 0 ? zero_table_rows : num_nodes;
   if (zero_rows_count > 0) {
     const bool fuse = work && zero_count == 0 && feature_dim % 4 == 0 &&
                       feature_dim / 4 <= 32 && aligned(zero_table, 16) &&
-                      num_nodes <= 0x7fffffffLL;
+                      ztable_rows <= 0x7fffffffLL;
     if (fuse) {
       ztable4 = reinterpret_cast<float4*>(zero_table);
     } else {
-      const int st0 = fsa_zero_rows_f32(zero_table, num_nodes, feature_dim, zero_rows,
+      const int st0 = fsa_zero_rows_f32(zero_table, ztable_rows, feature_dim, zero_rows,
                                         zero_rows_count, stream);
       if (st0 != FSA_OK) return st0;
     }
@@ -1848,7 +1850,7 @@ static int forward_2hop(const int32_t* rowptr, const int32_t* col, int64_t num_n
                      win2, next, fill4, fill_vec4, kSmemRoots, ztable4,
                      ztable4 != nullptr ? zero_rows : nullptr,
                      ztable4 != nullptr ? zero_rows_count : 0,
-                     static_cast<int>(feature_dim / 4), static_cast<uint32_t>(num_nodes)};
+                     static_cast<int>(feature_dim / 4), static_cast<uint32_t>(ztable_rows)};
   const int dsmem = kDrawTableBytes + kRprePad + (fill_vec4 > 0 ? kZeroBytes : 0);
   st = launch_dependent(fsa_2hop_draw_kernel, dgrid, kThreadsDraw, dsmem, s, da);
   if (st == FSA_OK) st = pe.mark(3, s);
@@ -1949,6 +1951,28 @@ int fsa_sample_agg_2hop_forward_sharded(const int32_t* rowptr, const int32_t* co
   return forward_2hop(rowptr, col, num_nodes, num_edges, t.base[0], feature_dim, frontier,
                       batch_size, batch_offset, fanout1, fanout2, seed, out, samples1, samples2,
                       workspace, workspace_bytes, zero_fill, zero_count, stream, &t);
+}
+
+int fsa_sample_agg_2hop_forward_sharded_zero_rows(
+    const int32_t* rowptr, const int32_t* col, int64_t num_nodes, int64_t num_edges,
+    const float* const* x_shards, int64_t shard_rows, int32_t num_shards, int64_t feature_dim,
+    const int32_t* frontier, int64_t batch_size, int64_t batch_offset, int32_t fanout1,
+    int32_t fanout2, uint64_t seed, float* out, int32_t* samples1, int32_t* samples2,
+    void* workspace, size_t workspace_bytes, float* zero_table, int64_t zero_table_rows,
+    const int32_t* zero_rows, int64_t zero_rows_count, void* stream) {
+  RowShards t;
+  if (num_nodes < 0 || feature_dim < 0 || zero_table_rows < 0 || zero_rows_count < 0 ||
+      (zero_rows_count > 0 && zero_rows == nullptr) ||
+      (zero_rows_count > 0 && zero_table_rows > 0 && feature_dim > 0 && zero_table == nullptr)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  const int st = make_shards(const_cast<float* const*>(x_shards), shard_rows, num_shards,
+                             num_nodes, feature_dim, &t);
+  if (st != FSA_OK) return st;
+  return forward_2hop(rowptr, col, num_nodes, num_edges, t.base[0], feature_dim, frontier,
+                      batch_size, batch_offset, fanout1, fanout2, seed, out, samples1, samples2,
+                      workspace, workspace_bytes, nullptr, 0, stream, &t, zero_table, zero_rows,
+                      zero_rows_count, zero_table_rows);
 }
 
 static int backward_2hop(const float* grad_out, const int32_t* samples1,
@@ -2460,6 +2484,8 @@ struct PullArgs {
   int64_t stride;
   int64_t ids_bytes;
   int64_t staged_bytes;  // bytes of each record copied to shared memory (ids, or the whole record)
+  int32_t* touched;      // optional [cap_roots * num_shards][k1 * k2]: per unit, the local row
+                         // of every owned id, -1 elsewhere
 };
 
 // Records up to this size are copied to shared memory whole (ids and
@@ -2506,13 +2532,20 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   const int ds = static_cast<int>(step - db * W);
   int64_t b = blockIdx.x / W;
   int s = static_cast<int>(blockIdx.x - b * W);
+  const int k12 = k1 * k2;
   for (; b < a.cap_roots; b += db, s += ds) {
     if (s >= W) {
       s -= W;
       ++b;
       if (b >= a.cap_roots) break;
     }
-    if (b >= s_roots[s]) continue;  // the same for the whole CTA
+    int32_t* tl = a.touched != nullptr ? a.touched + (b * W + s) * k12 : nullptr;
+    if (b >= s_roots[s]) {  // the same for the whole CTA
+      if (tl != nullptr) {
+        for (int e = tid; e < k12; e += nthreads) tl[e] = -1;
+      }
+      continue;
+    }
     const unsigned char* rec = a.regions[s] + kExchangeHeader + b * a.stride;
     {
       const int4* src = reinterpret_cast<const int4*>(rec);
@@ -2525,13 +2558,17 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
       int own = 0;
       for (int j = 0; j < k2; ++j) {
         const int32_t leaf = ids[k1 + i * k2 + j];
-        if (leaf < 0) continue;
-        ++cnt;
-        if (leaf >= N) {
-          flag_status(FSA_STATUS_BAD_NEIGHBOR);
-        } else if (static_cast<uint64_t>(leaf - lo) < rows) {
-          owned[i * k2 + own++] = static_cast<int>(leaf - lo);
+        int32_t row = -1;
+        if (leaf >= 0) {
+          ++cnt;
+          if (leaf >= N) {
+            flag_status(FSA_STATUS_BAD_NEIGHBOR);
+          } else if (static_cast<uint64_t>(leaf - lo) < rows) {
+            row = static_cast<int32_t>(leaf - lo);
+            owned[i * k2 + own++] = row;
+          }
         }
+        if (tl != nullptr) tl[i * k2 + j] = row;
       }
       valid[i] = cnt;
       mine[i] = own;
@@ -2628,13 +2665,20 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
   const int64_t u0 = static_cast<int64_t>(blockIdx.x) * nwarps + warp;
   int64_t b = u0 / W;
   int s = static_cast<int>(u0 - b * W);
+  const int k12 = k1 * k2;
   for (; b < a.cap_roots; b += db, s += ds) {
     if (s >= W) {
       s -= W;
       ++b;
       if (b >= a.cap_roots) break;
     }
-    if (b >= s_roots[s]) continue;  // the same for the whole warp
+    int32_t* tl = a.touched != nullptr ? a.touched + (b * W + s) * k12 : nullptr;
+    if (b >= s_roots[s]) {  // the same for the whole warp
+      if (tl != nullptr) {
+        for (int e = lane; e < k12; e += 32) tl[e] = -1;
+      }
+      continue;
+    }
     {
       const int4* src =
           reinterpret_cast<const int4*>(a.regions[s] + kExchangeHeader + b * a.stride);
@@ -2654,16 +2698,19 @@ __global__ void __launch_bounds__(kThreadsPull, kPullCtasPerSm)
       const int dj = 32 - di * k2;
       int i = lane / k2;
       int j = lane - i * k2;
-      for (int e = lane; e < k1 * k2; e += 32) {
+      for (int e = lane; e < k12; e += 32) {
         const int32_t leaf = ids[k1 + e];
+        int32_t row = -1;
         if (leaf >= 0) {
           atomicAdd(&valid[i], 1);
           if (leaf >= N) {
             flag_status(FSA_STATUS_BAD_NEIGHBOR);
           } else if (static_cast<uint64_t>(leaf - lo) < rows) {
-            owned[i * k2 + atomicAdd(&mine[i], 1)] = static_cast<int>(leaf - lo);
+            row = static_cast<int32_t>(leaf - lo);
+            owned[i * k2 + atomicAdd(&mine[i], 1)] = row;
           }
         }
+        if (tl != nullptr) tl[e] = row;
         i += di;
         j += dj;
         if (j >= k2) {
@@ -2761,7 +2808,8 @@ int fsa_sample_agg_2hop_backward_sharded_pull(const void* const* exchanges,
                                               int32_t shard, float* grad_shard,
                                               int64_t shard_rows, int64_t num_nodes,
                                               int64_t feature_dim, int32_t fanout1,
-                                              int32_t fanout2, void* stream) {
+                                              int32_t fanout2, int32_t* touched_rows,
+                                              int64_t touched_capacity, void* stream) {
   if (!exchange_args_ok(0, fanout1, fanout2, feature_dim) || exchanges == nullptr ||
       num_shards < 1 || num_shards > FSA_MAX_SHARDS || shard < 0 || shard >= num_shards ||
       shard_rows < 1 || shard_rows > 0x7fffffffLL || num_nodes < 0 ||
@@ -2780,6 +2828,11 @@ int fsa_sample_agg_2hop_backward_sharded_pull(const void* const* exchanges,
   const int64_t stride = exchange_root_bytes(fanout1, fanout2, feature_dim);
   pa.cap_roots = (static_cast<int64_t>(exchange_bytes) - kExchangeHeader) / stride;
   if (pa.cap_roots == 0) return FSA_OK;
+  if (touched_rows != nullptr &&
+      touched_capacity < pa.cap_roots * num_shards * fanout1 * static_cast<int64_t>(fanout2)) {
+    return FSA_ERR_INVALID_ARGUMENT;
+  }
+  pa.touched = touched_rows;
   pa.num_shards = num_shards;
   pa.shard = shard;
   pa.grad = grad_shard;

@@ -126,7 +126,8 @@ class ShardedFeatures:
     fit the region on every rank.
     """
 
-    def __init__(self, local: torch.Tensor, num_nodes: int, group=None, exchange_bytes: int = 0):
+    def __init__(self, local: torch.Tensor, num_nodes: int, group=None, exchange_bytes: int = 0,
+                 persistent: bool = False):
         import ctypes
 
         import torch.distributed as dist
@@ -158,6 +159,12 @@ class ShardedFeatures:
         # owner-computed backward when there is an exchange region (the same
         # setting on every rank: set it to False on all ranks for the push)
         self.pull = self.exchange is not None
+        # with the owner-computed backward: keep `grad` across steps and clear
+        # only the rows the previous backward touched (listed by it) instead
+        # of zero-filling the shard in every forward
+        self.persistent = bool(persistent)
+        self._touched = None          # int32 list of local rows (or -1) written by the pull
+        self._touched_valid = False   # the list names every row the last backward touched
         self._flag = torch.zeros(1, device=self.local.device)
         self._device = self.local.device.index
         ptrs, self._mapped = _ipc_share(
@@ -217,6 +224,15 @@ def _backward_pull(feats: ShardedFeatures, g, s1, s2):
                            f"region of {need} bytes; this ShardedFeatures has "
                            f"{feats.exchange_bytes}")
     stream = _stream_handle(g.device)
+    touched, capacity = None, 0
+    if feats.persistent:
+        # one entry per (region, record, slot, position) the pull can visit
+        per_root = int(L.fsa_exchange_bytes(1, k1, k2, D)) - 256
+        capacity = max((feats.exchange_bytes - 256) // per_root, 0) * feats.world * k1 * k2
+        if feats._touched is None or feats._touched.numel() < capacity:
+            feats._touched = torch.full((max(capacity, 1),), -1, dtype=torch.int32,
+                                        device=g.device)
+        touched = feats._touched
     _lib.check(L.fsa_sharded_publish_2hop(feats.exchange.data_ptr(), feats.exchange_bytes,
                                           g.data_ptr(), s1.data_ptr(), s2.data_ptr(), B, D, k1,
                                           k2, stream), "fsa_sharded_publish_2hop")
@@ -224,12 +240,14 @@ def _backward_pull(feats: ShardedFeatures, g, s1, s2):
     feats.device_barrier()
     _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
         feats.exchange_ptrs, feats.exchange_bytes, feats.world, feats.rank, feats.grad.data_ptr(),
-        feats.shard_rows, feats.num_nodes, D, k1, k2, stream),
+        feats.shard_rows, feats.num_nodes, D, k1, k2,
+        touched.data_ptr() if touched is not None else None, capacity, stream),
         "fsa_sample_agg_2hop_backward_sharded_pull")
+    feats._touched_valid = touched is not None
 
 
 def _forward_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier, fanout1, fanout2,
-                          seed, capture, batch_offset, zero):
+                          seed, capture, batch_offset, zero, clear_rows=None):
     from . import _as_int64, _as_seed, _check_fanout_2hop, _check_offset, _DeviceGuard
     from . import _lib, _ptr, _stream_handle
 
@@ -252,6 +270,10 @@ def _forward_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier, fanout1
             s2 = torch.full((B, fanout1, fanout2), -1, dtype=torch.int32, device=dev)
             if zero is not None:
                 zero.zero_()
+            if clear_rows is not None:
+                _lib.check(L.fsa_zero_rows_f32(feats.grad.data_ptr(), feats.grad.size(0), D,
+                                               clear_rows.data_ptr(), clear_rows.numel(),
+                                               _stream_handle(dev)), "fsa_zero_rows_f32")
             return out, s1, s2
         out = torch.empty((B, D), dtype=torch.float32, device=dev)
         s1 = torch.empty((B, fanout1), dtype=torch.int32, device=dev) if capture else None
@@ -259,12 +281,23 @@ def _forward_2hop_sharded(rowptr, col, feats: ShardedFeatures, frontier, fanout1
         ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, int(capture),
                                                         int(capture))
         ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
-        st = L.fsa_sample_agg_2hop_forward_sharded(
-            rowptr.data_ptr(), col.data_ptr(), feats.num_nodes, col.numel(), feats.x_ptrs,
-            feats.shard_rows, feats.world, D, frontier.data_ptr(), B, off, fanout1, fanout2,
-            seed, out.data_ptr(), _ptr(s1), _ptr(s2), ws.data_ptr(), ws_bytes, _ptr(zero),
-            zero.numel() if zero is not None else 0, _stream_handle(dev))
-        _lib.check(st, "fsa_sample_agg_2hop_forward_sharded")
+        if clear_rows is not None:
+            # the rows the previous backward touched, zeroed inside the
+            # sampling kernel (no dense fill)
+            st = L.fsa_sample_agg_2hop_forward_sharded_zero_rows(
+                rowptr.data_ptr(), col.data_ptr(), feats.num_nodes, col.numel(), feats.x_ptrs,
+                feats.shard_rows, feats.world, D, frontier.data_ptr(), B, off, fanout1, fanout2,
+                seed, out.data_ptr(), _ptr(s1), _ptr(s2), ws.data_ptr(), ws_bytes,
+                feats.grad.data_ptr(), feats.grad.size(0), clear_rows.data_ptr(),
+                clear_rows.numel(), _stream_handle(dev))
+            _lib.check(st, "fsa_sample_agg_2hop_forward_sharded_zero_rows")
+        else:
+            st = L.fsa_sample_agg_2hop_forward_sharded(
+                rowptr.data_ptr(), col.data_ptr(), feats.num_nodes, col.numel(), feats.x_ptrs,
+                feats.shard_rows, feats.world, D, frontier.data_ptr(), B, off, fanout1, fanout2,
+                seed, out.data_ptr(), _ptr(s1), _ptr(s2), ws.data_ptr(), ws_bytes, _ptr(zero),
+                zero.numel() if zero is not None else 0, _stream_handle(dev))
+            _lib.check(st, "fsa_sample_agg_2hop_forward_sharded")
     return out, s1, s2
 
 
@@ -273,10 +306,16 @@ class _Sharded2HopFn(torch.autograd.Function):
     def forward(ctx, local, rowptr, col, frontier, fanout1, fanout2, replay_seed, batch_offset,
                 feats):
         capture = local.requires_grad
+        pull = feats.pull and feats.exchange is not None
+        # persistent shard: clear the rows the last backward touched instead
+        # of zero-filling the whole shard (needs that backward's list)
+        clear = (feats._touched if capture and pull and feats.persistent
+                 and feats._touched_valid else None)
         out, s1, s2 = _forward_2hop_sharded(rowptr.contiguous(), col.contiguous(), feats,
                                             frontier.contiguous(), fanout1, fanout2,
                                             replay_seed, capture, batch_offset,
-                                            feats.grad if capture else None)
+                                            feats.grad if capture and clear is None else None,
+                                            clear)
         if capture:
             if not (feats.pull and feats.exchange is not None):
                 # every rank's gradient shard is zero before any rank's
@@ -306,6 +345,7 @@ class _Sharded2HopFn(torch.autograd.Function):
                         s2.size(2), feats.grad_ptrs, feats.shard_rows, feats.world,
                         feats.num_nodes, _stream_handle(g.device))
                     _lib.check(st, "fsa_sample_agg_2hop_backward_sharded")
+                    feats._touched_valid = False  # the list no longer names the touched rows
             # every rank's additions into this rank's shard are complete (and,
             # owner-computed, every rank has read the exchange regions before
             # any rank's next backward rewrites its own)
@@ -467,7 +507,7 @@ class _Exchange2HopFn(torch.autograd.Function):
             # one shard of all N rows: every contribution of every rank is this rank's
             _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
                 ex.exchange_ptrs, ex.exchange_bytes, ex.world, 0, grad.data_ptr(), ex.num_nodes,
-                ex.num_nodes, D, k1, k2, stream), "fsa_sample_agg_2hop_backward_sharded_pull")
+                ex.num_nodes, D, k1, k2, None, 0, stream), "fsa_sample_agg_2hop_backward_sharded_pull")
             ex.device_barrier()  # every rank has read the regions before they are rewritten
         return (grad,) + (None,) * 8
 

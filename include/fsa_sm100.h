@@ -277,7 +277,30 @@ FSA_API int fsa_sample_agg_2hop_backward_sharded_pull(const void* const* exchang
                                                       int32_t shard, float* grad_shard,
                                                       int64_t shard_rows, int64_t num_nodes,
                                                       int64_t feature_dim, int32_t fanout1,
-                                                      int32_t fanout2, void* stream);
+                                                      int32_t fanout2, int32_t* touched_rows,
+                                                      int64_t touched_capacity, void* stream);
+
+/*
+ * Persistent gradient shards for the owner-computed backward.  With
+ * touched_rows non-NULL (touched_capacity >= records per region *
+ * num_shards * fanout1 * fanout2 int32, records per region =
+ * (exchange_bytes - 256) / (fsa_exchange_bytes(1, ...) - 256)), the pull
+ * call also writes, for every (region, root) unit, the local row of each id
+ * it added (-1 for the others): the rows of grad_shard this step touched.
+ * fsa_sample_agg_2hop_forward_sharded_zero_rows is the sharded forward
+ * that, instead of zero-filling the whole gradient shard, zeroes the rows
+ * listed in zero_rows (entries outside [0, zero_table_rows) skipped) --
+ * inside its sampling kernel when the rows are whole float4 vectors of at
+ * most 32 -- so that a shard kept across steps holds only the current
+ * step's gradient after its backward.
+ */
+FSA_API int fsa_sample_agg_2hop_forward_sharded_zero_rows(
+    const int32_t* rowptr, const int32_t* col, int64_t num_nodes, int64_t num_edges,
+    const float* const* x_shards, int64_t shard_rows, int32_t num_shards, int64_t feature_dim,
+    const int32_t* frontier, int64_t batch_size, int64_t batch_offset, int32_t fanout1,
+    int32_t fanout2, uint64_t seed, float* out, int32_t* samples1, int32_t* samples2,
+    void* workspace, size_t workspace_bytes, float* zero_table, int64_t zero_table_rows,
+    const int32_t* zero_rows, int64_t zero_rows_count, void* stream);
 
 /*
  * Sharing shards between processes (one process per GPU), no counterpart in

@@ -224,11 +224,14 @@ def test_exchange_entry_points_reject_bad_arguments_before_cuda():
                                       NULL) == _lib.FSA_ERR_INVALID_ARGUMENT  # no gradient
     ptrs = (ctypes.c_void_p * 2)(fake, fake)
     pull = L.fsa_sample_agg_2hop_backward_sharded_pull
-    assert pull(ptrs, 1 << 20, 2, 2, fake, 10, 20, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
-    assert pull(ptrs, 1 << 20, 2, 0, fake, 10, 21, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
-    assert pull(ptrs, 100, 2, 0, fake, 10, 20, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert pull(ptrs, 1 << 20, 2, 2, fake, 10, 20, 8, 3, 2, NULL, 0, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert pull(ptrs, 1 << 20, 2, 0, fake, 10, 21, 8, 3, 2, NULL, 0, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert pull(ptrs, 100, 2, 0, fake, 10, 20, 8, 3, 2, NULL, 0, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
     bad = (ctypes.c_void_p * 2)(fake, None)
-    assert pull(bad, 1 << 20, 2, 0, fake, 10, 20, 8, 3, 2, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
+    assert pull(bad, 1 << 20, 2, 0, fake, 10, 20, 8, 3, 2, NULL, 0, NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
     # nothing to add: returns before any CUDA call
-    assert pull(ptrs, 1 << 20, 2, 0, fake, 10, 20, 8, 0, 2, NULL) == _lib.FSA_OK
+    assert pull(ptrs, 1 << 20, 2, 0, fake, 10, 20, 8, 0, 2, NULL, 0, NULL) == _lib.FSA_OK
+    # a touched-row list smaller than regions x records x f1 x f2
+    assert pull(ptrs, 256 + 16 * (32 + 32), 2, 0, fake, 10, 20, 8, 3, 2, fake, 10,
+                NULL) == _lib.FSA_ERR_INVALID_ARGUMENT
 

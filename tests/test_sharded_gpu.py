@@ -2,8 +2,9 @@
 peer mappings): the sharded 2-hop op must give the ids and outputs of the
 unsharded op on the whole table bit for bit, and its gradient shards must
 equal the rows of the all-reduced unsharded gradient (rtol 1e-5 / atol
-1e-6), with the backward sent as remote red.adds (push) and computed by the
-owners from the exchange regions (pull).  Skipped with fewer than two GPUs;
+1e-6), with the backward sent as remote red.adds (push), computed by the
+owners from the exchange regions (pull), and with the shard kept across
+steps and only its touched rows cleared (persistent).  Skipped with fewer than two GPUs;
 host-side pieces are also covered on the CPU."""
 
 from __future__ import annotations
@@ -39,7 +40,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, dim, fans, pull, results):
+def _worker(rank, world, port, dim, fans, mode, results):
     import numpy as np  # noqa: F401
     import torch.distributed as dist
 
@@ -64,11 +65,12 @@ def _worker(rank, world, port, dim, fans, pull, results):
         roots = synthetic.root_batch(n, 256, seed=3, device=dev)
         mine, off = sharding.local_roots(roots, rank, world)
         k1, k2 = fans
-        ex = sharding.exchange_bytes(-(-256 // world), k1, k2, dim) if pull else 0
-        feats = sharding.ShardedFeatures(local, n, exchange_bytes=ex)
+        ex = sharding.exchange_bytes(-(-256 // world), k1, k2, dim) if mode != "push" else 0
+        feats = sharding.ShardedFeatures(local, n, exchange_bytes=ex,
+                                         persistent=mode == "persistent")
         go = synthetic.features(mine.numel(), dim, seed=5 + rank, device=dev)
         ok = True
-        for step in range(2):  # two steps: the gradient shard is re-zeroed
+        for step in range(3):  # the shard is re-zeroed (or its touched rows cleared) each step
             out = sharding.fused_sample_agg_2hop_sharded(rp, cl, feats, mine, k1, k2,
                                                          replay_seed=17 + step,
                                                          batch_offset=off)
@@ -97,9 +99,9 @@ def _worker(rank, world, port, dim, fans, pull, results):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("pull", [False, True], ids=["push", "pull"])
+@pytest.mark.parametrize("mode", ["push", "pull", "persistent"])
 @pytest.mark.parametrize("dim,fans", [(64, (15, 10)), (33, (8, 4))])
-def test_sharded_two_gpus_match_unsharded(dim, fans, pull):
+def test_sharded_two_gpus_match_unsharded(dim, fans, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -107,7 +109,7 @@ def test_sharded_two_gpus_match_unsharded(dim, fans, pull):
     world = 2
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.spawn(_worker, args=(world, _free_port(), dim, fans, pull, results), nprocs=world,
+        mp.spawn(_worker, args=(world, _free_port(), dim, fans, mode, results), nprocs=world,
                  join=True)
         assert dict(results) == {0: True, 1: True}
 

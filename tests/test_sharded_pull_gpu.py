@@ -68,7 +68,8 @@ def run(name, dim, k1, k2, batches, world):
     shards = torch.zeros(world * rows, dim, device="cuda")
     for r in range(world):
         _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
-            ptrs, need, world, r, shards[r * rows].data_ptr(), rows, n, dim, k1, k2, stream()),
+            ptrs, need, world, r, shards[r * rows].data_ptr(), rows, n, dim, k1, k2, None, 0,
+            stream()),
             "pull")
     want = torch.zeros(n, dim, device="cuda")
     for (s1, s2, go), b in zip(ranks, batches):
@@ -116,7 +117,7 @@ def test_one_shard_of_all_rows_sums_every_rank():
     ptrs = (ctypes.c_void_p * world)(*[r.data_ptr() for r in regions])
     got = torch.zeros(n, dim, device="cuda")
     _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
-        ptrs, need, world, 0, got.data_ptr(), n, n, dim, k1, k2, stream()), "pull")
+        ptrs, need, world, 0, got.data_ptr(), n, n, dim, k1, k2, None, 0, stream()), "pull")
     want = torch.zeros(n, dim, device="cuda")
     for (s1, s2, go), b in zip(ranks, batches):
         _lib.check(L.fsa_sample_agg_2hop_backward(go.data_ptr(), s1.data_ptr(), s2.data_ptr(), b,
@@ -124,3 +125,44 @@ def test_one_shard_of_all_rows_sums_every_rank():
                    "backward")
     torch.cuda.synchronize()
     torch.testing.assert_close(got, want, rtol=RTOL, atol=ATOL)
+
+
+def test_pull_lists_the_rows_it_touched():
+    """With a touched-row list the pull call also writes, per (region, root)
+    unit, the local row of every owned id (-1 for the others and for units
+    past a region's root count): the rows a persistent shard clears next."""
+    name, dim, k1, k2, batches = "powerlaw", 16, 8, 4, (64, 50, 64)
+    g, _, _ = graph(name)
+    n = g.num_nodes
+    world = len(batches)
+    rows = -(-n // world)
+    ranks = []
+    for r, batch in enumerate(batches):
+        s1, s2 = sample(name, dim, k1, k2, batch, 80 + r, r * 64)
+        ranks.append((s1, s2, synthetic.features(batch, dim, seed=3 + r, device="cuda")))
+    need = L.fsa_exchange_bytes(max(batches), k1, k2, dim)
+    regions = [torch.empty((need,), dtype=torch.uint8, device="cuda") for _ in range(world)]
+    for (s1, s2, go), reg, b in zip(ranks, regions, batches):
+        _lib.check(L.fsa_sharded_publish_2hop(reg.data_ptr(), need, go.data_ptr(), s1.data_ptr(),
+                                              s2.data_ptr(), b, dim, k1, k2, stream()), "publish")
+    ptrs = (ctypes.c_void_p * world)(*[r.data_ptr() for r in regions])
+    cap = (need - 256) // (L.fsa_exchange_bytes(1, k1, k2, dim) - 256)
+    shard = 1
+    touched = torch.full((cap * world * k1 * k2,), 12345, dtype=torch.int32, device="cuda")
+    grad = torch.zeros(rows, dim, device="cuda")
+    _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
+        ptrs, need, world, shard, grad.data_ptr(), rows, n, dim, k1, k2, touched.data_ptr(),
+        touched.numel(), stream()), "pull")
+    torch.cuda.synchronize()
+    got = touched.cpu().view(cap, world, k1 * k2)
+    lo = shard * rows
+    for s, (s1, s2, _) in enumerate(ranks):
+        ids = s2.cpu().view(-1, k1 * k2)
+        want = torch.where((ids >= lo) & (ids < lo + rows) & (ids < n), ids - lo,
+                           torch.full_like(ids, -1))
+        assert torch.equal(got[:ids.size(0), s], want)
+        assert bool((got[ids.size(0):, s] == -1).all())
+    # the listed rows are exactly the rows the call added into
+    listed = got[got >= 0].unique()
+    nonzero = (grad.cpu().abs().sum(1) > 0).nonzero().flatten().to(torch.int32)
+    assert set(nonzero.tolist()) <= set(listed.tolist())
