@@ -123,7 +123,11 @@ class ShardedFeatures:
     every rank adds the contributions to its own rows from all ranks'
     regions (fsa_sample_agg_2hop_backward_sharded_pull) instead of sending
     one red.add per remote contribution.  Every backward's batch must then
-    fit the region on every rank.
+    fit the region on every rank.  With ``persistent=True`` as well, `grad`
+    is kept across steps: each backward lists the rows it added into, and
+    the next forward zeroes only those (inside its sampling kernel) instead
+    of zero-filling the shard; after every backward `grad` still holds
+    exactly that step's gradient.
     """
 
     def __init__(self, local: torch.Tensor, num_nodes: int, group=None, exchange_bytes: int = 0,
