@@ -874,6 +874,25 @@ def exchange_leg(w, inp: Inputs, args, dist: Dist, base_ms_per_step: float) -> d
     launches0 = fsa.launch_count()
     ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
     launches = (fsa.launch_count() - launches0) * args.steps // (args.steps + args.warmup)
+    # the same steps with the gradient kept across steps in ex.grad (rows the
+    # previous backward touched cleared in the forward, no N x D fill), then
+    # one step's ex.grad against the exchanged gradient of the same batch
+    ex.persistent = True
+    pers_ms, _ = timed(make_step(Api, w, inp, batch_offset=True), args.steps, args.warmup, dist)
+    j = (args.warmup + args.steps) % len(inp.frontiers)
+    step_j = make_step(Api, w, inp, batch_offset=True)
+    step_j(j)
+    kept = ex.grad.clone()
+    ex.persistent = False
+    step_j(j)
+    torch.cuda.synchronize()
+    pers_ok = bool(torch.isclose(kept, x.grad, rtol=1e-5, atol=1e-6).all())
+    x.grad = None
+    del kept
+    ex.grad = None
+    torch.cuda.empty_cache()
+    pflag = torch.tensor([float(pers_ok)], device="cuda")
+    tdist.all_reduce(pflag, op=tdist.ReduceOp.MIN)
     ex.close()
     units = w.batch * dist.world * args.steps
     per_step = ms / args.steps
@@ -889,6 +908,11 @@ def exchange_leg(w, inp: Inputs, args, dist: Dist, base_ms_per_step: float) -> d
         "grad_check": "every rank's gradient vs the NCCL-all-reduced per-rank gradients, "
                       "rtol 1e-5 / atol 1e-6",
         "grad_max_abs_err_rank0": max_err,
+        "persistent_grad": {"value": units / (pers_ms / 1000.0),
+                            "ms_per_step": pers_ms / args.steps,
+                            "matches_exchanged_gradient": bool(pflag[0].item() == 1.0),
+                            "api": "GradientExchange(..., persistent=True): the gradient in "
+                                   "exchange.grad, touched rows cleared in the forward"},
         "mode": ("replicated features; the backward publishes this rank's saved ids and "
                  "upstream gradient in an exchange region mapped into every peer (CUDA IPC) and "
                  "adds every rank's contributions into this rank's gradient after a one-float "

@@ -392,9 +392,17 @@ class GradientExchange:
     NVLink carries (W - 1) * B * (4 (f1 + f1 f2) + 4 D) bytes per rank
     instead of the all-reduce's ~2 * 4 N D.  Construction and `close()` are
     collective.
+
+    With ``persistent=True`` the gradient lives in `grad` (one N x D tensor
+    for the exchange's lifetime, like `PersistentGradient`): the backward
+    adds into it and autograd produces no gradient for x; each backward lists
+    the rows it added into and the next forward zeroes only those (inside its
+    sampling kernel) instead of zero-filling N x D, so after every backward
+    `grad` holds exactly that step's global gradient.
     """
 
-    def __init__(self, num_nodes: int, dim: int, exchange_bytes: int, device=None, group=None):
+    def __init__(self, num_nodes: int, dim: int, exchange_bytes: int, device=None, group=None,
+                 persistent: bool = False):
         import torch.distributed as dist
 
         from . import _lib
@@ -413,6 +421,11 @@ class GradientExchange:
             dev = torch.device("cuda", torch.cuda.current_device())
         self.num_nodes, self.dim, self.exchange_bytes = int(num_nodes), int(dim), int(exchange_bytes)
         self.exchange = torch.empty((self.exchange_bytes,), dtype=torch.uint8, device=dev)
+        self.persistent = bool(persistent)
+        self.grad = (torch.zeros((self.num_nodes, self.dim), dtype=torch.float32, device=dev)
+                     if self.persistent else None)
+        self._touched = None
+        self._touched_valid = False
         self._flag = torch.zeros(1, device=dev)
         self._device = dev.index
         import ctypes
@@ -470,14 +483,29 @@ class _Exchange2HopFn(torch.autograd.Function):
             out = torch.empty((B, D), dtype=torch.float32, device=dev)
             s1 = torch.full((B, fanout1), -1, dtype=torch.int32, device=dev)
             s2 = torch.full((B, fanout1, fanout2), -1, dtype=torch.int32, device=dev)
-            grad = torch.empty_like(xc)
             ws_bytes = L.fsa_sample_agg_2hop_workspace_size(B, fanout1, fanout2, 1, 1)
             ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
-            _lib.check(L.fsa_sample_agg_2hop_forward(
-                rowptr.data_ptr(), col.data_ptr(), N, col.numel(), xc.data_ptr(), D,
-                frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(),
-                s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, grad.data_ptr(),
-                grad.numel(), _stream_handle(dev)), "fsa_sample_agg_2hop_forward")
+            stream = _stream_handle(dev)
+            if ex.persistent and ex.grad is None:  # switched on after construction
+                ex.grad = torch.zeros_like(xc)
+                ex._touched_valid = False
+            if ex.persistent and ex._touched_valid:
+                # the rows the previous backward added into, zeroed inside the
+                # sampling kernel (no N x D fill)
+                grad = ex.grad
+                _lib.check(L.fsa_sample_agg_2hop_forward_zero_rows(
+                    rowptr.data_ptr(), col.data_ptr(), N, col.numel(), xc.data_ptr(), D,
+                    frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(),
+                    s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, grad.data_ptr(),
+                    ex._touched.data_ptr(), ex._touched.numel(), stream),
+                    "fsa_sample_agg_2hop_forward_zero_rows")
+            else:
+                grad = ex.grad if ex.persistent else torch.empty_like(xc)
+                _lib.check(L.fsa_sample_agg_2hop_forward(
+                    rowptr.data_ptr(), col.data_ptr(), N, col.numel(), xc.data_ptr(), D,
+                    frontier.data_ptr(), B, off, fanout1, fanout2, seed, out.data_ptr(),
+                    s1.data_ptr(), s2.data_ptr(), ws.data_ptr(), ws_bytes, grad.data_ptr(),
+                    grad.numel(), stream), "fsa_sample_agg_2hop_forward")
             if fanout1 == 0 or fanout2 == 0:
                 out.zero_()  # nothing sampled (fuseop/binding.cpp:183-185)
         ctx.save_for_backward(s1, s2)
@@ -508,11 +536,23 @@ class _Exchange2HopFn(torch.autograd.Function):
                                                   g.data_ptr(), s1.data_ptr(), s2.data_ptr(), B,
                                                   D, k1, k2, stream), "fsa_sharded_publish_2hop")
             ex.device_barrier()  # every rank's region holds this step's records
+            touched, capacity = None, 0
+            if ex.persistent:
+                per_root = int(L.fsa_exchange_bytes(1, k1, k2, D)) - 256
+                capacity = max((ex.exchange_bytes - 256) // per_root, 0) * ex.world * k1 * k2
+                if ex._touched is None or ex._touched.numel() < capacity:
+                    ex._touched = torch.full((max(capacity, 1),), -1, dtype=torch.int32,
+                                             device=g.device)
+                touched = ex._touched
             # one shard of all N rows: every contribution of every rank is this rank's
             _lib.check(L.fsa_sample_agg_2hop_backward_sharded_pull(
                 ex.exchange_ptrs, ex.exchange_bytes, ex.world, 0, grad.data_ptr(), ex.num_nodes,
-                ex.num_nodes, D, k1, k2, None, 0, stream), "fsa_sample_agg_2hop_backward_sharded_pull")
+                ex.num_nodes, D, k1, k2, touched.data_ptr() if touched is not None else None,
+                capacity, stream), "fsa_sample_agg_2hop_backward_sharded_pull")
+            ex._touched_valid = touched is not None
             ex.device_barrier()  # every rank has read the regions before they are rewritten
+        if ex.persistent:
+            return (None,) * 9  # the gradient is in ex.grad
         return (grad,) + (None,) * 8
 
 

@@ -114,7 +114,7 @@ def test_sharded_two_gpus_match_unsharded(dim, fans, mode):
         assert dict(results) == {0: True, 1: True}
 
 
-def _exchange_worker(rank, world, port, results):
+def _exchange_worker(rank, world, port, persistent, results):
     import torch.distributed as dist
 
     import fusesampleagg_b200 as fsa
@@ -136,9 +136,10 @@ def _exchange_worker(rank, world, port, results):
         roots = synthetic.root_batch(n, 256, seed=4, device=dev)
         mine, off = sharding.local_roots(roots, rank, world)
         ex = sharding.GradientExchange(n, dim, sharding.exchange_bytes(-(-256 // world), k1, k2,
-                                                                        dim), device=dev)
+                                                                        dim), device=dev,
+                                       persistent=persistent)
         ok = True
-        for step in range(2):
+        for step in range(3):
             go = synthetic.features(mine.numel(), dim, seed=20 + 2 * rank + step, device=dev)
             xe = x.clone().requires_grad_(True)
             out = sharding.fused_sample_agg_2hop_exchange(rp, cl, xe, mine, k1, k2,
@@ -153,7 +154,9 @@ def _exchange_worker(rank, world, port, results):
             dist.all_reduce(full)
             torch.cuda.synchronize()
             ok &= torch.equal(out.view(torch.int32), ref.detach().view(torch.int32))
-            ok &= torch.allclose(xe.grad, full, rtol=RTOL, atol=ATOL)
+            got = ex.grad if persistent else xe.grad
+            ok &= (xe.grad is None) == persistent
+            ok &= torch.allclose(got, full, rtol=RTOL, atol=ATOL)
         results[rank] = bool(ok)
     finally:
         if ex is not None:
@@ -162,7 +165,8 @@ def _exchange_worker(rank, world, port, results):
 
 
 @pytest.mark.gpu
-def test_gradient_exchange_two_gpus_equals_allreduce():
+@pytest.mark.parametrize("persistent", [False, True], ids=["fresh", "persistent"])
+def test_gradient_exchange_two_gpus_equals_allreduce(persistent):
     """Replicated features: the exchange backward leaves every rank with the
     all-reduced gradient of the per-rank gradients."""
     if torch.cuda.device_count() < 2:
@@ -172,6 +176,7 @@ def test_gradient_exchange_two_gpus_equals_allreduce():
     world = 2
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.spawn(_exchange_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        mp.spawn(_exchange_worker, args=(world, _free_port(), persistent, results), nprocs=world,
+                 join=True)
         assert dict(results) == {0: True, 1: True}
 
